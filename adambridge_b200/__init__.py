@@ -1,0 +1,26 @@
+"""adambridge_b200: adambridge's fused AdamW / Lion optimizer-update hot path on B200.
+
+The optimizer state (FP32 or FP24 master weights, FP32 / BF16 / block-scaled FP8
+moments) lives in HBM and is updated by hand-written sm_100a kernels (libabx, C ABI in
+include/abx.h), behind the reference's ``AdamBridge`` / ``OptiComputeAdamW`` /
+``LionBridge`` API.  ``ZeroAdamBridge`` / ``ZeroLionBridge`` shard the state ZeRO-1
+style over the ranks of a process group and all-gather the new bf16 weights with NCCL.
+"""
+
+from . import native, precision
+from .engine import StepStats
+from .optimizer import AdamBridge, LionBridge, OptiComputeAdamW
+from .precision import bytes_per_param
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "AdamBridge",
+    "LionBridge",
+    "OptiComputeAdamW",
+    "StepStats",
+    "bytes_per_param",
+    "native",
+    "precision",
+    "__version__",
+]

@@ -1,0 +1,373 @@
+#!/usr/bin/env python
+"""Fused optimizer-step benchmark: Gparams/s and fraction of the HBM roofline on B200.
+
+Workload (BASELINE.json metric): a Llama-7B-shaped parameter set (hidden 4096, 32 layers, MLP 11008,
+vocab 32000, untied: 291 tensors, 6,738,415,616 parameters), bf16 weights with an fp32 master, AdamW with
+bf16 moments (stochastic rounding on), bf16 gradients.  One step = one optimizer step over every parameter:
+the fused update kernels (20 algorithmic bytes per parameter: master r/w 8, grad 2, m r/w 4, v r/w 4, bf16
+weight 2) plus, on N > 1 GPUs, the NCCL all-gather of the new bf16 weights (ZeRO-1, fixed model: strong
+scaling).  Synthetic data: weights ~ N(0, 0.02), gradients ~ N(0, 1e-3) from seeded generators.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl abx|reference]
+
+``--impl reference`` times the reference's own CPU kernel library (oracle/_ref, compiled from the
+reference sources) on the host cores, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LLAMA7B = dict(hidden=4096, layers=32, mlp=11008, vocab=32000, kv=4096)
+BYTES_PER_PARAM = {("adamw", "bf16"): 20, ("adamw", "fp32"): 28, ("adamw", "fp8"): 16.125,
+                   ("lion", "bf16"): 16, ("lion", "fp32"): 20, ("lion", "fp8"): 14.0625}
+
+
+def llama_shapes(hidden, layers, mlp, vocab, kv, tied=False):
+    """Parameter shapes in the optimizer order of a Llama decoder (embedding, layers, final norm, lm_head)."""
+    shapes = [(vocab, hidden)]
+    for _ in range(layers):
+        shapes += [(hidden, hidden), (kv, hidden), (kv, hidden), (hidden, hidden), (mlp, hidden), (mlp, hidden),
+                   (hidden, mlp), (hidden,), (hidden,)]
+    shapes.append((hidden,))
+    if not tied:
+        shapes.append((vocab, hidden))
+    return shapes
+
+
+def numel(shape):
+    n = 1
+    for d in shape:
+        n *= d
+    return n
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        else:
+            self.lines = []
+
+    def summary(self) -> dict:
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        mhz, mx, reasons = [], None, set()
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                mhz.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# --------------------------------------------------------------------------- CPU baseline
+
+def cpu_reference_sample(seconds: float = 10.0, steps: int | None = None, warmup: int = 1):
+    """Time the reference's own kernel library (oracle/_ref) -- or, where it was not built, the oracle port --
+    on one Llama-7B decoder layer's seven matrices (202,375,168 params; bf16 moments, bf16 grad and weights,
+    fp32 master), all host threads.  Returns (Gparams/s, threads, kind, sample description, ms per step)."""
+    import ctypes
+
+    import numpy as np
+
+    from oracle import oracle as O
+
+    ref = O.load_reference()
+    kind = "reference" if ref is not None else "port"
+    threads = len(os.sched_getaffinity(0)) if ref is not None else 1
+    h, mlp = LLAMA7B["hidden"], LLAMA7B["mlp"]
+    shapes = [(h, h)] * 4 + [(mlp, h)] * 3
+    if ref is None:
+        shapes = [(h, h)]   # the single-threaded port gets a smaller sample
+    rng = np.random.default_rng(0)
+    segs, keep = [], []
+    group = O.Group(lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, seed=0, stochastic=1)
+    for i, shp in enumerate(shapes):
+        n = numel(shp)
+        hs = O.HostSegment(n, O.DT_BF16, O.DT_BF16, O.DT_BF16, O.DT_F32, O.ADAMW, index=i)
+        hs.buffers = {"p": (rng.standard_normal(n, dtype=np.float32) * 0.02),
+                      "g": O.bf16_bits(rng.standard_normal(n, dtype=np.float32) * 1e-3),
+                      "m": np.zeros(n, np.uint16), "v": np.zeros(n, np.uint16), "out": np.zeros(n, np.uint16)}
+        keep.append(hs)
+        segs.append(hs.ctype(group))
+    total = sum(s.n for s in segs)
+    arr = O.seg_array(segs)
+    orc = None if ref is not None else O.load_oracle()
+
+    def one(step):
+        for s in segs:
+            s.step = step
+        rc = ref.multi_step_array(arr, threads) if ref is not None else orc.multi_step(segs, O.SIMD_AVX512)
+        if rc != 0:
+            raise RuntimeError(f"CPU baseline update failed ({rc})")
+
+    step = 0
+    for _ in range(warmup):
+        step += 1
+        one(step)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (steps is None and time.perf_counter() < t_end) or (steps is not None and len(times) < steps):
+        step += 1
+        t0 = time.perf_counter()
+        one(step)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    del keep
+    desc = (f"{len(shapes)} tensors of one Llama-7B layer ({total:,} params), AdamW bf16 moments, bf16 grad/out, "
+            f"{len(times)} steps, median; simd={O.SIMD_NAMES[ref.simd_level] if ref else 'port'}")
+    return total / med / 1e9, threads, kind, desc, med * 1e3
+
+
+def reference_arm(args, rank: int, world: int) -> None:
+    """--impl reference: the reference's CPU implementation on this host, rank 0 only."""
+    if rank != 0:
+        return
+    gps, threads, kind, desc, ms = cpu_reference_sample(steps=args.steps, warmup=args.warmup)
+    line = {"impl": "reference", "metric": "fused step Gparams/s (7B, bf16 moments)", "value": round(gps, 4),
+            "unit": "Gparams/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "llama7b-adamw-bf16-moments (CPU sample: one decoder layer)",
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(gps, 4), "unit": "Gparams/s", "cores": threads, "kind": kind,
+                             "sample": desc},
+            "e2e": {"value": round(gps, 4), "unit": "Gparams/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from adambridge_b200 import native
+    from adambridge_b200.zero import ZeroAdamBridge, ZeroLionBridge
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    kern = native.load()
+    dims = dict(LLAMA7B)
+    if args.layers is not None:
+        dims["layers"] = args.layers
+    if args.vocab is not None:
+        dims["vocab"] = args.vocab
+    shapes = llama_shapes(**dims)
+    n_params = sum(numel(s) for s in shapes)
+    algo, prec = args.algorithm, args.precision
+    bpp = BYTES_PER_PARAM[(algo, prec)]
+
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    params = []
+    with torch.no_grad():
+        for shp in shapes:
+            p = torch.empty(shp, dtype=torch.bfloat16, device=dev)
+            p.normal_(0.0, 0.02, generator=gen)
+            params.append(torch.nn.Parameter(p))
+    cls = ZeroLionBridge if algo == "lion" else ZeroAdamBridge
+    kw = dict(lr=1e-5, betas=(0.9, 0.99), weight_decay=0.1) if algo == "lion" else \
+        dict(lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    opt = cls(params, precision=prec, rounds=args.rounds, **kw)
+    L = opt.layout
+    shard_params = sum(pc.n for r in opt._pieces for pc in r)
+    with torch.no_grad():
+        opt.grad_shard.normal_(0.0, 1e-3, generator=gen)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    def step():
+        opt.step_shard()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    launches0 = kern.launch_count()
+    opt.trace = []
+    cur = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        t0.record(cur)
+        for _ in range(args.steps):
+            step()
+        t1.record(cur)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = kern.launch_count() - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    kernel_ms = sum(s.elapsed_time(e) for s, e in opt.trace) / args.steps
+    n_launches_trace = len(opt.trace)
+    opt.trace = None
+    ms_t = torch.tensor([ms, kernel_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max, kernel_ms_max = ms_t.tolist()
+
+    # ---- e2e: host buffers through the public API (pinned grad shard in, updated weight shard out)
+    e2e = None
+    if not args.no_e2e:
+        e2e_steps = max(1, min(args.steps, args.e2e_steps))
+        host_g = torch.empty(L.shard_numel, dtype=opt.grad_dtype, pin_memory=True)
+        host_g.copy_(opt.grad_shard.cpu())
+        mine = [opt.flat_weights[slice(*L.rank_range(r, rank))] for r in range(L.rounds)]
+        host_w = torch.empty(L.shard_numel, dtype=opt.dtype, pin_memory=True)
+
+        def e2e_step():
+            opt.grad_shard.copy_(host_g, non_blocking=True)
+            opt.step_shard()
+            for r, w in enumerate(mine):
+                host_w[r * L.chunk:(r + 1) * L.chunk].copy_(w, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        for _ in range(e2e_steps):
+            e2e_step()
+        b.record(cur)
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([a.elapsed_time(b) / e2e_steps], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e_ms = e_ms.item()
+        e2e = {"value": round(n_params / (e_ms / 1e3) / 1e9, 4), "unit": "Gparams/s",
+               "h2d_bytes_per_step": host_g.numel() * host_g.element_size(),
+               "d2h_bytes_per_step": host_w.numel() * host_w.element_size(), "ms_per_step": round(e_ms, 3),
+               "path": "ZeroAdamBridge.step_shard with the gradient shard copied in from pinned host memory and the "
+                       "updated weight shard copied out to pinned host memory every step"}
+        del host_g, host_w
+
+    if rank != 0:
+        return
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = bpp * shard_params / (kernel_ms_max / 1e3) / 1e9
+    line = {
+        "metric": "fused step Gparams/s and % of HBM roofline (7B, bf16 moments)" if (algo, prec) == ("adamw", "bf16")
+        else f"fused step Gparams/s ({algo}, {prec} moments)",
+        "value": round(n_params / (ms_max / 1e3) / 1e9, 4), "unit": "Gparams/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"llama7b-{algo}-{prec}-moments" if dims == LLAMA7B else
+                   f"llama-{dims['layers']}L-v{dims['vocab']}-{algo}-{prec}-moments", "params": n_params, "tensors": len(shapes),
+                   "weights": "bf16", "grads": "bf16", "master": "fp32", "stochastic_rounding": True,
+                   "parallelism": f"zero1-dp{world}", "rounds": L.rounds,
+                   "l2": "no flush: each step streams %.1f GB >> 126 MB L2" % (bpp * shard_params / 1e9)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "basis": f"{bpp} B/param x {shard_params:,} params per rank per step / update-kernel time "
+                              f"{kernel_ms_max:.3f} ms (CUDA events on the update stream, {n_launches_trace // args.steps} "
+                              f"multi-segment calls per step); peak = MEASURED_PEAKS.json hbm_gbs (of measured)"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if world > 1:
+        line["allgather"] = {"bytes_received_per_rank": int((world - 1) * L.chunk * L.rounds * 2),
+                             "step_ms": round(ms_max, 3), "update_kernel_ms": round(kernel_ms_max, 3)}
+    if world == 1 and not args.no_cpu_baseline:
+        gps, threads, kind, desc, _ = cpu_reference_sample(seconds=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(gps, 4), "unit": "Gparams/s", "cores": threads, "kind": kind,
+                                "sample": desc}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="abx", choices=["abx", "reference"])
+    ap.add_argument("--algorithm", default="adamw", choices=["adamw", "lion"])
+    ap.add_argument("--precision", default="bf16", choices=["fp32", "bf16", "fp8"])
+    ap.add_argument("--rounds", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None, help="override the decoder depth (small profiling cases)")
+    ap.add_argument("--vocab", type=int, default=None, help="override the vocabulary (small profiling cases)")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "abx":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return 0
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        gpu_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

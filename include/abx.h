@@ -1,0 +1,188 @@
+/*
+ * abx.h -- C ABI of libabx, the B200 (sm_100a) fused optimizer-update library.
+ *
+ * libabx replaces the host SIMD kernel library of adambridge
+ * (adambridge/csrc/adambridge_kernels.c) with CUDA kernels that update
+ * optimizer state resident in HBM.  The structs, dtype codes, algorithm codes
+ * and error codes below keep the reference's layout and meaning, so a binding
+ * written for the reference (adambridge/native.py:58-111) needs only its
+ * function names, its first argument (a CUDA stream instead of a thread pool)
+ * and its pointers (device instead of host memory) changed.
+ *
+ * Conventions shared by every entry point:
+ *   - Every pointer inside a segment is a DEVICE pointer on the current CUDA
+ *     device of the calling thread.  The caller owns all memory; the kernels
+ *     update p, m, v, the scales and out in place.
+ *   - `stream` is a cudaStream_t (NULL: the legacy default stream).  Work is
+ *     enqueued asynchronously; argument errors are returned synchronously
+ *     BEFORE anything is launched, and on such an error nothing is updated.
+ *   - Results are bit-identical to the reference's native kernels built for
+ *     the SIMD level selected with abx_set_simd_level (default AVX-512): the
+ *     reference fuses multiply-adds in its vector loop and not in its scalar
+ *     tail, and libabx reproduces exactly which elements take which path.
+ *   - No entry point allocates device memory; no entry point synchronizes.
+ */
+#ifndef ABX_H
+#define ABX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ABX_ABI_VERSION 1
+
+/* Element formats; same codes as the reference (adambridge_kernels.c:73, native.py:47-51). */
+enum {
+    ABX_DT_NONE = 0,  /* no buffer (out only) */
+    ABX_DT_F32  = 1,
+    ABX_DT_BF16 = 2,
+    ABX_DT_FP8  = 3,  /* moments: E4M3fn m, E5M2 sqrt(v), one fp32 scale per 128 elements */
+    ABX_DT_F24  = 4   /* master: bf16 hi plane + uint8 lo plane (top 24 bits of fp32) */
+};
+
+/* Update rules; same codes as the reference (adambridge_kernels.c:75). */
+enum { ABX_ALGO_ADAMW = 0, ABX_ALGO_LION = 1 };
+
+/* Rounding patterns of the reference's SIMD levels (adambridge_kernels.c:74).
+ * AVX-512 / AVX2 / NEON fuse the multiply-adds of their 16 / 8 / 4-lane loop and
+ * run the last n % lanes elements of a segment unfused; SCALAR fuses none. */
+enum { ABX_SIMD_SCALAR = 0, ABX_SIMD_AVX2 = 1, ABX_SIMD_AVX512 = 2, ABX_SIMD_NEON = 3 };
+
+#define ABX_FP8_BLOCK 128
+
+/* Error codes.  -1 .. -13 have the reference's meaning (check_segment,
+ * adambridge_kernels.c:1537-1553, and adambridge_multi_step :1611-1626). */
+#define ABX_OK                 0
+#define ABX_E_ARG             -1   /* NULL segment array / negative n / NULL hparams */
+#define ABX_E_NULL_PTR        -2   /* a required buffer is NULL */
+#define ABX_E_G_DTYPE         -3
+#define ABX_E_MV_DTYPE        -4
+#define ABX_E_OUT_DTYPE       -5
+#define ABX_E_OUT_NULL        -6
+#define ABX_E_SCALE_NULL      -7   /* FP8 moments without scales */
+#define ABX_E_GROUP_NULL      -8
+#define ABX_E_TOO_MANY        -9
+#define ABX_E_OOM            -10
+#define ABX_E_OFFSET         -11   /* negative offset, or FP8 offset not a multiple of 128 */
+#define ABX_E_ALGO           -12
+#define ABX_E_P_DTYPE        -13
+/* libabx-specific */
+#define ABX_E_CUDA           -20   /* a CUDA runtime call failed; see abx_last_error() */
+#define ABX_E_ALIGN          -21   /* a buffer is not aligned to its element size */
+#define ABX_E_SIMD_LEVEL     -22   /* unknown SIMD level */
+
+/* Per-step coefficients (adambridge_hparams, adambridge_kernels.c:77-88). */
+typedef struct abx_hparams {
+    float beta1;
+    float beta2;
+    float one_minus_beta1;
+    float one_minus_beta2;
+    float decay;         /* 1 - lr * weight_decay */
+    float step_size;     /* AdamW: lr / (1 - beta1^t); Lion: lr */
+    float inv_sqrt_bc2;  /* 1 / sqrt(1 - beta2^t) */
+    float eps;
+    uint32_t seed;       /* stochastic-rounding stream of this (param, step) */
+    int32_t stochastic;  /* nonzero: stochastic rounding of bf16/fp8 moments and the fp24 master */
+} abx_hparams;
+
+/* Hyperparameters of one parameter group (adambridge_group, adambridge_kernels.c:736-745). */
+typedef struct abx_group {
+    double lr;
+    double beta1;
+    double beta2;
+    double eps;
+    double weight_decay;
+    uint64_t seed;       /* base seed for stochastic rounding */
+    int32_t stochastic;
+    int32_t reserved;
+} abx_group;
+
+/* One tensor (or a 128-aligned chunk of one) to update (adambridge_segment,
+ * adambridge_kernels.c:747-769).  All pointers are device pointers. */
+typedef struct abx_segment {
+    void* p;                 /* master: fp32 values, or the fp24 hi plane (uint16) when p_dtype is ABX_DT_F24 */
+    uint8_t* p_lo;           /* fp24 only: the lo plane */
+    const void* g;           /* gradient, g_dtype */
+    void* m;                 /* first moment, mv_dtype (FP8: E4M3 codes, padded to whole 128-blocks) */
+    void* v;                 /* second moment (FP8: E5M2 codes of sqrt(v)); unused by Lion */
+    float* m_scale;          /* FP8 only: one scale per 128 elements */
+    float* v_scale;
+    void* out;               /* optional copy of the stored master in out_dtype (the model's weights) */
+    const abx_group* group;  /* host pointer; read by abx_multi_step only */
+    int64_t n;
+    int64_t step;            /* this update's step number (the caller increments it) */
+    uint64_t index;          /* parameter index: selects the rounding stream */
+    int64_t offset;          /* element offset of p[0] within its parameter (FP8: a multiple of 128) */
+    int32_t g_dtype;
+    int32_t mv_dtype;
+    int32_t out_dtype;
+    int32_t algorithm;
+    int32_t p_dtype;         /* ABX_DT_F32 (or 0) or ABX_DT_F24 */
+    int32_t reserved;
+} abx_segment;
+
+/* ---- version and layout probes (replace adambridge_kernels.c:1493-1514) ---- */
+int abx_abi_version(void);
+int abx_hparams_size(void);
+int abx_group_size(void);
+int abx_segment_size(void);
+
+/* ---- rounding pattern (replaces adambridge_set_simd_level / _simd_level /
+ *      _detected_simd_level, adambridge_kernels.c:1495-1510) ----
+ * Selects which reference build the kernels reproduce bit for bit.  Any level
+ * may be chosen (it is an emulation target, not a CPU feature); -1 restores the
+ * default, AVX-512.  Returns the level now active, or ABX_E_SIMD_LEVEL. */
+int abx_set_simd_level(int level);
+int abx_simd_level(void);
+int abx_detected_simd_level(void);   /* the default level: ABX_SIMD_AVX512 */
+
+/* ---- host-side coefficient and seed computation (adambridge_kernels.c:773-809),
+ *      exposed so bindings and tests can check them ---- */
+uint32_t abx_step_seed(uint64_t base_seed, uint64_t index, int64_t step);
+int abx_hparams_for(const abx_segment* seg, abx_hparams* out);
+
+/* ---- updates ----
+ * abx_multi_step (replaces adambridge_multi_step, adambridge_kernels.c:1611):
+ *   validates every segment, derives each one's coefficients from its group and
+ *   step in double precision, and enqueues the updates on `stream`.  Segments of
+ *   any size, dtype mix and algorithm may be mixed; one kernel launch covers up
+ *   to 64 segments of one dtype combination.  `max_ctas` caps the CTAs per launch
+ *   (0: one wave of resident CTAs on every SM); it plays the role of the
+ *   reference's `threads` argument, leaving SMs to concurrent work.
+ * abx_multi_apply (replaces adambridge_multi_apply, :1630): the same with
+ *   caller-supplied coefficients hps[i] for segs[i]; groups and steps are ignored.
+ * abx_multi_step_scaled / abx_multi_apply_scaled: as above, and every gradient
+ *   element is first multiplied by the device scalar *g_scale (gradient clipping
+ *   or loss unscaling fused into the update); a bf16 gradient is rounded back to
+ *   bf16 after the multiply, as an in-place torch multiply would leave it.
+ *   g_scale NULL means 1.  Not in the reference: its callers scale the
+ *   gradient in place before calling it.
+ */
+int abx_multi_step(void* stream, abx_segment* const* segs, int32_t nsegs, int32_t max_ctas);
+int abx_multi_apply(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t nsegs,
+                    int32_t max_ctas);
+int abx_multi_step_scaled(void* stream, abx_segment* const* segs, int32_t nsegs, int32_t max_ctas,
+                          const float* g_scale);
+int abx_multi_apply_scaled(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t nsegs,
+                           int32_t max_ctas, const float* g_scale);
+
+/* Single-tensor AdamW with fp32/bf16 moments and an fp32 master (replaces
+ * adambridge_fused_adamw, adambridge_kernels.c:1518, same argument meaning and
+ * error codes, plus the stream). */
+int abx_fused_adamw(float* p, const void* g, int g_dtype, void* m, void* v, int mv_dtype, void* out,
+                    int out_dtype, int64_t n, uint64_t offset, const abx_hparams* hp, void* stream);
+
+/* Kernel launches this library has made in this process, all threads and devices. */
+uint64_t abx_launch_count(void);
+
+/* Message of the last ABX_E_CUDA / ABX_E_ALIGN error on this thread (never NULL). */
+const char* abx_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ABX_H */
