@@ -130,6 +130,38 @@ __device__ __forceinline__ float adamw_elem_sel(float p, float g, float& m, floa
     return fused ? adamw_elem<true>(p, g, m, v, c) : adamw_elem<false>(p, g, m, v, c);
 }
 
+// The same, also returning sqrt(new v): the FP8 path re-encodes v as sqrt(v), and for v >= 0 that is the
+// square root the update already took (the reference takes it twice, csrc:454 and :1000).
+template <bool FUSED>
+__device__ __forceinline__ float adamw_elem_sq(float p, float g, float& m, float& v, float& sq, const Coef& c)
+{
+    p = __fmul_rn(p, c.decay);
+    if (FUSED) {
+        m = __fmaf_rn(c.b1, m, __fmul_rn(c.omb1, g));
+        v = __fmaf_rn(c.b2, v, __fmul_rn(c.omb2, __fmul_rn(g, g)));
+        sq = __fsqrt_rn(v);
+        return __fmaf_rn(-c.step, __fdiv_rn(m, __fmaf_rn(sq, c.isbc2, c.eps)), p);
+    } else {
+        m = __fadd_rn(__fmul_rn(c.b1, m), __fmul_rn(c.omb1, g));
+        v = __fadd_rn(__fmul_rn(c.b2, v), __fmul_rn(c.omb2, __fmul_rn(g, g)));
+        sq = __fsqrt_rn(v);
+        return __fsub_rn(p, __fmul_rn(c.step, __fdiv_rn(m, __fadd_rn(__fmul_rn(sq, c.isbc2), c.eps))));
+    }
+}
+
+// Two floats -> packed bf16 pair (lo in the low half), round-to-nearest-even by the hardware conversion.
+// Identical to bf16_rne for every non-NaN input; every NaN reaching it was produced by GPU arithmetic
+// (the canonical 0x7fffffff), which both map to 0x7fff.
+__device__ __forceinline__ uint32_t pack_bf16_rne(float lo, float hi)
+{
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+// High halves of two 32-bit words -> one word (lo's half in the low 16 bits).
+__device__ __forceinline__ uint32_t pack_hi16(uint32_t lo, uint32_t hi) { return __byte_perm(lo, hi, 0x7632); }
+
 // Lion on one element: c = b1 m + (1-b1) g; p = p decay - lr sign(c); m = b2 m + (1-b2) g,
 // each multiply-add fused; sign(0) = sign(NaN) = 0.
 __device__ __forceinline__ float lion_elem(float p, float g, float& m, const Coef& c)

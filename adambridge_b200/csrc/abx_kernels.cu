@@ -3,18 +3,27 @@
 //
 // Design (one pass over HBM, bandwidth-bound; no tensor cores):
 //   * A launch covers up to kMaxSegs segments of one (algorithm, moment format,
-//     master format) combination.  Their descriptors travel by value in the
-//     kernel parameters (__grid_constant__), so a launch needs no device-side
-//     table, no host->device copy and no allocation.
+//     master format, gradient format) combination.  Their descriptors travel by
+//     value in the kernel parameters (__grid_constant__): no device-side table,
+//     no host->device copy, no allocation.
 //   * Each segment is cut into tiles of kTile = 2048 elements; the tiles of all
-//     segments form one index space that a persistent grid (one wave of resident
-//     CTAs on every SM) walks with a grid stride.  A CTA finds a tile's segment by
-//     a binary search over the descriptors' first-tile indices.
-//   * A thread owns 8 consecutive elements of a tile: 16-byte vector loads and
-//     stores for every fp32/bf16 array (two for fp32), 8-byte ones for byte
-//     arrays, so each warp moves whole 512-byte (bf16) or 1 KB (fp32) lines.
-//   * FP8 moments: a 128-element block is exactly 16 threads (half a warp); the
-//     block maxima for the new scales are reduced with four xor-shuffles.
+//     segments form one index space that a persistent grid walks with a grid
+//     stride.  A CTA finds a tile's segment by a binary search over the
+//     descriptors' first-tile indices.
+//   * Inside a CTA, one producer warp streams whole tiles of every input array
+//     (master, gradient, moments) into a ring of shared-memory stages with 1-D
+//     TMA bulk copies (cp.async.bulk ... mbarrier::complete_tx), so the bytes in
+//     flight per SM are set by the ring, not by registers or occupancy.  Eight
+//     consumer warps compute from shared memory and store results straight to
+//     HBM with vector stores.  Tiles that cannot be bulk-copied (the partial last
+//     tile of a segment, unaligned buffers) are read directly from HBM.
+//   * A consumer thread owns two groups of 4 consecutive elements per tile
+//     (elements 4t..4t+3 and 1024+4t..), so every shared-memory read and every
+//     global store of a warp covers one contiguous span without bank conflicts.
+//     With FP8 moments one 128-element block is exactly one warp's group; the
+//     block maxima for the new scales are reduced with xor-shuffles.
+//   * Every mbarrier wait is bounded: a wait that gives up sets a device status
+//     word (read by abx_pipeline_status) and the CTA drains its copies and exits.
 //
 // Bit-exactness with the reference (adambridge/csrc/adambridge_kernels.c) is
 // obtained by restating every operation with an explicit rounding intrinsic and
@@ -36,12 +45,19 @@
 
 namespace abx {
 
-constexpr int kThreads = 256;
-constexpr int kVec = 8;                  // elements per thread per tile
-constexpr int kTile = kThreads * kVec;   // elements per CTA per tile
-constexpr int kMaxSegs = 64;             // segments per launch (parameter block ~9.8 KB)
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;   // + one producer warp
+constexpr int kGroup = 4;                              // elements per thread per half tile
+constexpr int kHalf = kConsumerWarps * 32 * kGroup;    // 1024
+constexpr int kTile = 2 * kHalf;                       // 2048 elements per tile
+constexpr int kMaxSegs = 64;                           // segments per launch (parameter block ~10 KB)
+constexpr int kSmemTarget = 72 * 1024;                 // ring bytes per CTA (about three CTAs per SM)
+constexpr uint32_t kSpinLimit = 1u << 22;              // mbarrier polls before a wait gives up
 
-// Device copy of one segment with its per-step coefficients (152 bytes).
+// Set (OR) by a CTA whose pipeline wait gave up; never set in correct operation.
+__device__ unsigned int g_pipeline_status;
+
+// Device copy of one segment with its per-step coefficients.
 struct KSeg {
     const void* g;
     void* p;
@@ -57,343 +73,417 @@ struct KSeg {
     Coef c;
     uint32_t s_m, s_v, s_p;   // rounding streams of m, v and the fp24 master
     uint32_t off32;           // (uint32) element offset of p[0] within its parameter
-    int32_t g_dt, out_dt;
+    int32_t out_dt;
     int32_t sr;
-    int32_t vec_ok;           // every buffer aligned for 16-byte (8-byte for bytes) vector access
+    int32_t vec_ok;           // 4-element vector access is aligned in every buffer (direct path)
+    int32_t tma_ok;           // every streamed buffer is 16-byte aligned (bulk-copy path)
 };
 
 template <int NSEG>
 struct KArgs {
     int32_t nseg;
-    int32_t pad;
+    int32_t stages;
     int64_t total_tiles;
     const float* g_scale;     // optional device scalar multiplying every gradient element
     KSeg seg[NSEG];
 };
 
-// ---- 8-element loads and stores -----------------------------------------------------
-// Vector path when the thread's 8 elements are all valid and the segment is aligned;
-// otherwise element by element (tails and unaligned callers).
+// Shared-memory layout of one pipeline stage for a kernel kind (every array a whole tile).
+template <int ALGO, int MV, int PT, int GT>
+struct Cfg {
+    static constexpr int PB = PT == ABX_DT_F24 ? 2 : 4;
+    static constexpr int LB = PT == ABX_DT_F24 ? 1 : 0;
+    static constexpr int GB = GT == ABX_DT_BF16 ? 2 : 4;
+    static constexpr int MB = MV == ABX_DT_F32 ? 4 : (MV == ABX_DT_BF16 ? 2 : 1);
+    static constexpr int VB = ALGO == ABX_ALGO_LION ? 0 : MB;
+    static constexpr int OFF_P = 0;
+    static constexpr int OFF_L = OFF_P + kTile * PB;
+    static constexpr int OFF_G = OFF_L + kTile * LB;
+    static constexpr int OFF_M = OFF_G + kTile * GB;
+    static constexpr int OFF_V = OFF_M + kTile * MB;
+    static constexpr int STAGE = OFF_V + kTile * VB;
+};
 
-__device__ __forceinline__ void ld8_f32(const float* p, int cnt, bool vec, float (&x)[8])
+// ---- PTX: mbarriers and 1-D TMA bulk copies -----------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
 {
-    if (vec && cnt == 8) {
-        const float4 a = *reinterpret_cast<const float4*>(p);
-        const float4 b = *reinterpret_cast<const float4*>(p + 4);
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase of `bar` with parity `parity`; false (and the status word set) if it never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
+{
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(&g_pipeline_status, 1u);
+    return false;
+}
+
+// Global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+
+// ---- 4-element loads and stores -----------------------------------------------------
+// Source: the staged tile in shared memory (s != nullptr: always 4 valid, aligned
+// elements), else global memory -- one vector when the thread's 4 elements are valid
+// and the segment is aligned, element by element otherwise.
+
+__device__ __forceinline__ void ld4_f32(const float* g, const float* s, int cnt, bool vec, float (&x)[4])
+{
+    if (s != nullptr) {
+        const float4 a = *reinterpret_cast<const float4*>(s);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    } else if (vec && cnt == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(g);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
     } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = k < cnt ? p[k] : 0.0f;
+        for (int k = 0; k < 4; ++k) x[k] = k < cnt ? g[k] : 0.0f;
     }
 }
 
-__device__ __forceinline__ void ld8_bf16(const uint16_t* p, int cnt, bool vec, float (&x)[8])
+// 4 bf16 values as two packed words (element 2j in the low half of w[j]).
+__device__ __forceinline__ void ld4_b16(const uint16_t* g, const uint16_t* s, int cnt, bool vec, uint32_t (&w)[2])
 {
-    if (vec && cnt == 8) {
-        const uint4 a = *reinterpret_cast<const uint4*>(p);
-        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) { x[2 * j] = u2f(w[j] << 16); x[2 * j + 1] = u2f(w[j] & 0xffff0000U); }
+    if (s != nullptr) {
+        const uint2 a = *reinterpret_cast<const uint2*>(s);
+        w[0] = a.x; w[1] = a.y;
+    } else if (vec && cnt == 4) {
+        const uint2 a = *reinterpret_cast<const uint2*>(g);
+        w[0] = a.x; w[1] = a.y;
     } else {
+        uint32_t h[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = k < cnt ? u2f((uint32_t)p[k] << 16) : 0.0f;
+        for (int k = 0; k < 4; ++k) h[k] = k < cnt ? g[k] : 0U;
+        w[0] = h[0] | (h[1] << 16);
+        w[1] = h[2] | (h[3] << 16);
     }
 }
 
-// Gradient in its own dtype, read through the non-coherent path (read-only during the kernel).
-__device__ __forceinline__ void ld8_grad(const void* g, int dt, int cnt, bool vec, float (&x)[8])
+__device__ __forceinline__ uint32_t ld4_b8(const uint8_t* g, const uint8_t* s, int cnt, bool vec)
 {
-    if (dt == ABX_DT_BF16) {
-        const uint16_t* p = static_cast<const uint16_t*>(g);
-        if (vec && cnt == 8) {
-            const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+    if (s != nullptr) return *reinterpret_cast<const uint32_t*>(s);
+    if (vec && cnt == 4) return *reinterpret_cast<const uint32_t*>(g);
+    uint32_t w = 0;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) { x[2 * j] = u2f(w[j] << 16); x[2 * j + 1] = u2f(w[j] & 0xffff0000U); }
-        } else {
+    for (int k = 0; k < 4; ++k) w |= (k < cnt ? (uint32_t)g[k] : 0U) << (8 * k);
+    return w;
+}
+
+__device__ __forceinline__ void st4_f32(float* g, int cnt, bool vec, const float (&x)[4])
+{
+    if (vec && cnt == 4) {
+        *reinterpret_cast<float4*>(g) = make_float4(x[0], x[1], x[2], x[3]);
+    } else {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) x[k] = k < cnt ? u2f((uint32_t)__ldg(p + k) << 16) : 0.0f;
+        for (int k = 0; k < 4; ++k) if (k < cnt) g[k] = x[k];
+    }
+}
+
+__device__ __forceinline__ void st4_b16(uint16_t* g, int cnt, bool vec, uint32_t w0, uint32_t w1)
+{
+    if (vec && cnt == 4) {
+        *reinterpret_cast<uint2*>(g) = make_uint2(w0, w1);
+    } else {
+        const uint32_t h[4] = {w0 & 0xffffU, w0 >> 16, w1 & 0xffffU, w1 >> 16};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) if (k < cnt) g[k] = (uint16_t)h[k];
+    }
+}
+
+__device__ __forceinline__ void st4_b8(uint8_t* g, int cnt, bool vec, uint32_t w)
+{
+    if (vec && cnt == 4) {
+        *reinterpret_cast<uint32_t*>(g) = w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) if (k < cnt) g[k] = (uint8_t)(w >> (8 * k));
+    }
+}
+
+__device__ __forceinline__ void unpack_b16(const uint32_t (&w)[2], float (&x)[4])
+{
+    x[0] = u2f(w[0] << 16); x[1] = u2f(w[0] & 0xffff0000U);
+    x[2] = u2f(w[1] << 16); x[3] = u2f(w[1] & 0xffff0000U);
+}
+
+// ---- typed element groups ------------------------------------------------------------
+
+// Gradient with the optional clip / unscale factor (a bf16 gradient is rounded back to bf16,
+// as torch's in-place multiply of a bf16 tensor leaves it).
+template <int GT>
+__device__ __forceinline__ void grad4(const KSeg& S, int64_t i0, int cnt, const uint8_t* s, const float* gs,
+                                      float (&g)[4])
+{
+    if constexpr (GT == ABX_DT_BF16) {
+        uint32_t w[2];
+        ld4_b16(static_cast<const uint16_t*>(S.g) + i0, reinterpret_cast<const uint16_t*>(s), cnt, S.vec_ok, w);
+        unpack_b16(w, g);
+    } else {
+        ld4_f32(static_cast<const float*>(S.g) + i0, reinterpret_cast<const float*>(s), cnt, S.vec_ok, g);
+    }
+    if (gs != nullptr) {
+        const float f = *gs;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            g[k] = __fmul_rn(g[k], f);
+            if constexpr (GT == ABX_DT_BF16) g[k] = u2f(bf16_rne(f2u(g[k])) & 0xffff0000U);
         }
-    } else {
-        const float* p = static_cast<const float*>(g);
-        if (vec && cnt == 8) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
-            x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-        } else {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) x[k] = k < cnt ? __ldg(p + k) : 0.0f;
-        }
     }
 }
-
-__device__ __forceinline__ void st8_f32(float* p, int cnt, bool vec, const float (&x)[8])
-{
-    if (vec && cnt == 8) {
-        *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
-        *reinterpret_cast<float4*>(p + 4) = make_float4(x[4], x[5], x[6], x[7]);
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) if (k < cnt) p[k] = x[k];
-    }
-}
-
-// Stores 8 16-bit values given in the low halves of h[].
-__device__ __forceinline__ void st8_u16(uint16_t* p, int cnt, bool vec, const uint32_t (&h)[8])
-{
-    if (vec && cnt == 8) {
-        *reinterpret_cast<uint4*>(p) = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
-                                                  h[6] | (h[7] << 16));
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) if (k < cnt) p[k] = (uint16_t)h[k];
-    }
-}
-
-__device__ __forceinline__ void ld8_u8(const uint8_t* p, int cnt, bool vec, uint32_t (&c)[8])
-{
-    if (vec && cnt == 8) {
-        const uint2 a = *reinterpret_cast<const uint2*>(p);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) { c[k] = (a.x >> (8 * k)) & 0xffU; c[4 + k] = (a.y >> (8 * k)) & 0xffU; }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) c[k] = k < cnt ? p[k] : 0U;
-    }
-}
-
-__device__ __forceinline__ void st8_u8(uint8_t* p, int cnt, bool vec, const uint32_t (&c)[8])
-{
-    if (vec && cnt == 8) {
-        *reinterpret_cast<uint2*>(p) = make_uint2(c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24),
-                                                  c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24));
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) if (k < cnt) p[k] = (uint8_t)c[k];
-    }
-}
-
-// ---- master and out ---------------------------------------------------------------
 
 template <int PT>
-__device__ __forceinline__ void ld8_master(const KSeg& S, int64_t i0, int cnt, bool vec, float (&p)[8])
+__device__ __forceinline__ void master4(const KSeg& S, int64_t i0, int cnt, const uint8_t* sp, const uint8_t* sl,
+                                        float (&p)[4])
 {
     if constexpr (PT == ABX_DT_F24) {
-        float hi[8];
-        uint32_t lo[8];
-        ld8_bf16(static_cast<const uint16_t*>(S.p) + i0, cnt, vec, hi);
-        ld8_u8(S.p_lo + i0, cnt, vec, lo);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = u2f(f2u(hi[k]) | (lo[k] << 8));
+        uint32_t w[2];
+        ld4_b16(static_cast<const uint16_t*>(S.p) + i0, reinterpret_cast<const uint16_t*>(sp), cnt, S.vec_ok, w);
+        const uint32_t lo = ld4_b8(S.p_lo + i0, sl, cnt, S.vec_ok);
+        p[0] = u2f((w[0] << 16) | ((lo & 0xffU) << 8));
+        p[1] = u2f((w[0] & 0xffff0000U) | (lo & 0xff00U));
+        p[2] = u2f((w[1] << 16) | ((lo >> 8) & 0xff00U));
+        p[3] = u2f((w[1] & 0xffff0000U) | ((lo >> 16) & 0xff00U));
     } else {
-        ld8_f32(static_cast<const float*>(S.p) + i0, cnt, vec, p);
+        ld4_f32(static_cast<const float*>(S.p) + i0, reinterpret_cast<const float*>(sp), cnt, S.vec_ok, p);
     }
 }
 
 // Round (fp24) and store the new master values; p[] becomes the values stored.
-template <int PT>
-__device__ __forceinline__ void st8_master(const KSeg& S, int64_t i0, int cnt, bool vec, float (&p)[8])
+template <int PT, bool SR>
+__device__ __forceinline__ void store_master4(const KSeg& S, int64_t i0, int cnt, float (&p)[4])
 {
     if constexpr (PT == ABX_DT_F24) {
-        uint32_t hi[8], lo[8];
-        const bool sr = S.sr != 0;
+        uint32_t b[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t r = sr ? hash32((S.off32 + (uint32_t)(i0 + k)) ^ S.s_p) : 0U;
-            const uint32_t b = f24_bits(f2u(p[k]), sr, r);
-            hi[k] = b >> 16;
-            lo[k] = (b >> 8) & 0xffU;
-            p[k] = u2f(b);
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t r = SR ? hash32((S.off32 + (uint32_t)(i0 + k)) ^ S.s_p) : 0U;
+            b[k] = f24_bits(f2u(p[k]), SR, r);
+            p[k] = u2f(b[k]);
         }
-        st8_u16(static_cast<uint16_t*>(S.p) + i0, cnt, vec, hi);
-        st8_u8(S.p_lo + i0, cnt, vec, lo);
+        // lo plane: byte 1 of each word, packed in element order
+        const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0051), __byte_perm(b[2], b[3], 0x0051), 0x5410);
+        st4_b16(static_cast<uint16_t*>(S.p) + i0, cnt, S.vec_ok, pack_hi16(b[0], b[1]), pack_hi16(b[2], b[3]));
+        st4_b8(S.p_lo + i0, cnt, S.vec_ok, lo);
     } else {
-        st8_f32(static_cast<float*>(S.p) + i0, cnt, vec, p);
+        st4_f32(static_cast<float*>(S.p) + i0, cnt, S.vec_ok, p);
     }
 }
 
-__device__ __forceinline__ void st8_out(const KSeg& S, int64_t i0, int cnt, bool vec, const float (&p)[8])
+__device__ __forceinline__ void store_out4(const KSeg& S, int64_t i0, int cnt, const float (&p)[4])
 {
     if (S.out_dt == ABX_DT_BF16) {
-        uint32_t h[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) h[k] = bf16_rne(f2u(p[k])) >> 16;
-        st8_u16(static_cast<uint16_t*>(S.out) + i0, cnt, vec, h);
+        st4_b16(static_cast<uint16_t*>(S.out) + i0, cnt, S.vec_ok, pack_bf16_rne(p[0], p[1]), pack_bf16_rne(p[2], p[3]));
     } else if (S.out_dt == ABX_DT_F32) {
-        st8_f32(static_cast<float*>(S.out) + i0, cnt, vec, p);
+        st4_f32(static_cast<float*>(S.out) + i0, cnt, S.vec_ok, p);
     }
 }
 
-// Gradient with the optional clip / unscale factor (a bf16 gradient is rounded back
-// to bf16, as torch's in-place multiply of a bf16 tensor leaves it).
-__device__ __forceinline__ void ld8_scaled_grad(const KSeg& S, int64_t i0, int cnt, bool vec, const float* gs,
-                                                float (&g)[8])
-{
-    const int elem = S.g_dt == ABX_DT_BF16 ? 2 : 4;
-    ld8_grad(static_cast<const char*>(S.g) + i0 * elem, S.g_dt, cnt, vec, g);
-    if (gs != nullptr) {
-        const float s = *gs;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            g[k] = __fmul_rn(g[k], s);
-            if (S.g_dt == ABX_DT_BF16) g[k] = u2f(bf16_rne(f2u(g[k])) & 0xffff0000U);
-        }
-    }
-}
-
-// Moments in fp32 or bf16 (dense layouts).
 template <int MV>
-__device__ __forceinline__ void ld8_moment(const void* base, int64_t i0, int cnt, bool vec, float (&x)[8])
-{
-    if constexpr (MV == ABX_DT_BF16) ld8_bf16(static_cast<const uint16_t*>(base) + i0, cnt, vec, x);
-    else ld8_f32(static_cast<const float*>(base) + i0, cnt, vec, x);
-}
-
-template <int MV>
-__device__ __forceinline__ void st8_moment(void* base, int64_t i0, int cnt, bool vec, const float (&x)[8], bool sr,
-                                           uint32_t seed, uint32_t idx0)
+__device__ __forceinline__ void moment4(const void* base, int64_t i0, int cnt, bool vec, const uint8_t* s,
+                                        float (&x)[4])
 {
     if constexpr (MV == ABX_DT_BF16) {
-        uint32_t h[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) h[k] = bf16_store_bits(x[k], sr, sr ? hash32((idx0 + (uint32_t)k) ^ seed) : 0U);
-        st8_u16(static_cast<uint16_t*>(base) + i0, cnt, vec, h);
+        uint32_t w[2];
+        ld4_b16(static_cast<const uint16_t*>(base) + i0, reinterpret_cast<const uint16_t*>(s), cnt, vec, w);
+        unpack_b16(w, x);
     } else {
-        st8_f32(static_cast<float*>(base) + i0, cnt, vec, x);
+        ld4_f32(static_cast<const float*>(base) + i0, reinterpret_cast<const float*>(s), cnt, vec, x);
     }
 }
 
-// ---- one thread's 8 elements ---------------------------------------------------------
-
-template <int ALGO, int MV, int PT>
-__device__ __forceinline__ void update8_dense(const KSeg& S, int64_t i0, const float* gs)
+// A bf16 moment: stochastic -- 16 random bits added below the kept half, then truncated -- or nearest-even.
+template <int MV, bool SR>
+__device__ __forceinline__ void store_moment4(void* base, int64_t i0, int cnt, bool vec, const float (&x)[4],
+                                              uint32_t seed, uint32_t idx0)
 {
-    const int64_t left = S.n - i0;
-    if (left <= 0) return;
-    const int cnt = left < kVec ? (int)left : kVec;
-    const bool vec = S.vec_ok != 0;
-    float g[8], p[8], m[8];
-    ld8_scaled_grad(S, i0, cnt, vec, gs, g);
-    ld8_master<PT>(S, i0, cnt, vec, p);
-    ld8_moment<MV>(S.m, i0, cnt, vec, m);
-    const Coef c = S.c;
-    const bool sr = S.sr != 0;
-    const uint32_t idx0 = S.off32 + (uint32_t)i0;
-    if constexpr (ALGO == ABX_ALGO_LION) {
+    if constexpr (MV == ABX_DT_BF16) {
+        uint32_t w0, w1;
+        if constexpr (SR) {
+            uint32_t b[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = lion_elem(p[k], g[k], m[k], c);
-        st8_master<PT>(S, i0, cnt, vec, p);
-        st8_moment<MV>(S.m, i0, cnt, vec, m, sr, S.s_m, idx0);
-    } else {
-        float v[8];
-        ld8_moment<MV>(S.v, i0, cnt, vec, v);
-        if (i0 + kVec <= S.fused_end) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) p[k] = adamw_elem<true>(p[k], g[k], m[k], v[k], c);
+            for (int k = 0; k < 4; ++k) b[k] = f2u(x[k]) + (hash32((idx0 + (uint32_t)k) ^ seed) & 0xffffU);
+            w0 = pack_hi16(b[0], b[1]);
+            w1 = pack_hi16(b[2], b[3]);
         } else {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) p[k] = adamw_elem_sel(p[k], g[k], m[k], v[k], c, i0 + k < S.fused_end);
+            w0 = pack_bf16_rne(x[0], x[1]);
+            w1 = pack_bf16_rne(x[2], x[3]);
         }
-        st8_master<PT>(S, i0, cnt, vec, p);
-        st8_moment<MV>(S.m, i0, cnt, vec, m, sr, S.s_m, idx0);
-        st8_moment<MV>(S.v, i0, cnt, vec, v, sr, S.s_v, idx0);
+        st4_b16(static_cast<uint16_t*>(base) + i0, cnt, vec, w0, w1);
+    } else {
+        st4_f32(static_cast<float*>(base) + i0, cnt, vec, x);
     }
-    st8_out(S, i0, cnt, vec, p);
 }
 
-// Max over the 16 lanes holding one 128-element block (lanes 0-15 or 16-31 of a warp).
-__device__ __forceinline__ float block_max16(float x)
+// ---- one tile ------------------------------------------------------------------------------
+
+// FP32 / BF16 moments: each consumer thread updates its two groups of 4 elements.
+template <int ALGO, int MV, int PT, int GT, bool SR>
+__device__ __forceinline__ void tile_dense(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+{
+    using C = Cfg<ALGO, MV, PT, GT>;
+    const Coef c = S.c;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e0 = h * kHalf + threadIdx.x * kGroup;
+        const int64_t i0 = base + e0;
+        const int64_t left = S.n - i0;
+        if (left <= 0) continue;
+        const int cnt = left < kGroup ? (int)left : kGroup;
+        const uint32_t idx0 = S.off32 + (uint32_t)i0;
+        float g[4], p[4], m[4];
+        grad4<GT>(S, i0, cnt, st ? st + C::OFF_G + e0 * C::GB : nullptr, gs, g);
+        master4<PT>(S, i0, cnt, st ? st + C::OFF_P + e0 * C::PB : nullptr, st ? st + C::OFF_L + e0 : nullptr, p);
+        moment4<MV>(S.m, i0, cnt, S.vec_ok, st ? st + C::OFF_M + e0 * C::MB : nullptr, m);
+        if constexpr (ALGO == ABX_ALGO_LION) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) p[k] = lion_elem(p[k], g[k], m[k], c);
+            store_master4<PT, SR>(S, i0, cnt, p);
+            store_moment4<MV, SR>(S.m, i0, cnt, S.vec_ok, m, S.s_m, idx0);
+        } else {
+            float v[4];
+            moment4<MV>(S.v, i0, cnt, S.vec_ok, st ? st + C::OFF_V + e0 * C::MB : nullptr, v);
+            if (i0 + kGroup <= S.fused_end) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) p[k] = adamw_elem<true>(p[k], g[k], m[k], v[k], c);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) p[k] = adamw_elem_sel(p[k], g[k], m[k], v[k], c, i0 + k < S.fused_end);
+            }
+            store_master4<PT, SR>(S, i0, cnt, p);
+            store_moment4<MV, SR>(S.m, i0, cnt, S.vec_ok, m, S.s_m, idx0);
+            store_moment4<MV, SR>(S.v, i0, cnt, S.vec_ok, v, S.s_v, idx0);
+        }
+        store_out4(S, i0, cnt, p);
+    }
+}
+
+__device__ __forceinline__ float warp_max(float x)
 {
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffU, x, o));
+    for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffU, x, o));
     return x;
 }
 
-// FP8 moments.  Called by every lane of a warp whose first element is inside the
-// segment (the shuffles need the whole warp); lanes of a half-warp whose block
-// starts past the end touch no memory.
-template <int ALGO, int PT>
-__device__ __forceinline__ void update8_fp8(const KSeg& S, int64_t i0, const float* gs)
+// FP8 moments: in each half tile, warp w owns block w (128 elements, 4 per lane).  Called by whole
+// warps; a warp whose block starts past the end of the segment skips it (the test is warp-uniform).
+template <int ALGO, int PT, int GT, bool SR>
+__device__ __forceinline__ void tile_fp8(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
 {
-    const int lane16 = threadIdx.x & 15;
-    const int64_t b0 = i0 - lane16 * kVec;          // start of this half-warp's block
-    const bool blk_ok = b0 < S.n;
-    const int64_t left = S.n - i0;
-    const int cnt = left <= 0 ? 0 : (left < kVec ? (int)left : kVec);
-    const bool vec = S.vec_ok != 0;
-    const int64_t blk = b0 >> 7;
+    using C = Cfg<ALGO, ABX_DT_FP8, PT, GT>;
     const Coef c = S.c;
-    const bool sr = S.sr != 0;
-    const uint32_t idx0 = S.off32 + (uint32_t)i0;
-
-    float g[8], p[8], mt[8];
-    uint32_t mc[8];
-    const float sm = blk_ok ? S.m_scale[blk] : 1.0f;
-    ld8_u8(static_cast<const uint8_t*>(S.m) + i0, blk_ok ? 8 : 0, vec, mc);
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) mt[k] = __fmul_rn(dec_e4m3(mc[k]), sm);
-    ld8_scaled_grad(S, i0, cnt, vec, gs, g);
-    ld8_master<PT>(S, i0, cnt, vec, p);
-
-    if constexpr (ALGO == ABX_ALGO_LION) {
+    for (int h = 0; h < 2; ++h) {
+        const int e0 = h * kHalf + threadIdx.x * kGroup;
+        const int64_t i0 = base + e0;
+        const int64_t b0 = i0 - lane * kGroup;      // start of this warp's block
+        if (b0 >= S.n) continue;
+        const int64_t blk = b0 >> 7;
+        const int64_t left = S.n - i0;
+        const int cnt = left <= 0 ? 0 : (left < kGroup ? (int)left : kGroup);
+        const uint32_t idx0 = S.off32 + (uint32_t)i0;
+        // the codes of the whole block exist (the buffer is padded to whole blocks): always 4 here
+        const uint32_t mc = ld4_b8(static_cast<const uint8_t*>(S.m) + i0, st ? st + C::OFF_M + e0 : nullptr, 4, S.vec_ok);
+        const float sm = S.m_scale[blk];
+        float g[4], p[4], mt[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = lion_elem(p[k], g[k], mt[k], c);
-        st8_master<PT>(S, i0, cnt, vec, p);
-        st8_out(S, i0, cnt, vec, p);
-        float am = 0.0f;
+        for (int k = 0; k < 4; ++k) mt[k] = __fmul_rn(dec_e4m3((mc >> (8 * k)) & 0xffU), sm);
+        grad4<GT>(S, i0, cnt, st ? st + C::OFF_G + e0 * C::GB : nullptr, gs, g);
+        master4<PT>(S, i0, cnt, st ? st + C::OFF_P + e0 * C::PB : nullptr, st ? st + C::OFF_L + e0 : nullptr, p);
+        if constexpr (ALGO == ABX_ALGO_LION) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) { const float a = fabsf(mt[k]); am = (k < cnt && a > am) ? a : am; }
-        am = block_max16(am);
-        const float scm = am > 0.0f ? __fdiv_rn(am, 448.0f) : 1.0f;
-        if (blk_ok) {
+            for (int k = 0; k < 4; ++k) p[k] = lion_elem(p[k], g[k], mt[k], c);
+            store_master4<PT, SR>(S, i0, cnt, p);
+            store_out4(S, i0, cnt, p);
+            float am = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-                mc[k] = k < cnt ? enc_e4m3(__fdiv_rn(mt[k], scm), sr, sr ? hash32((idx0 + (uint32_t)k) ^ S.s_m) : 0U) : 0U;
-            st8_u8(static_cast<uint8_t*>(S.m) + i0, 8, vec, mc);
-            if (lane16 == 0) S.m_scale[blk] = scm;
+            for (int k = 0; k < 4; ++k) { const float a = fabsf(mt[k]); am = (k < cnt && a > am) ? a : am; }
+            am = warp_max(am);
+            const float scm = am > 0.0f ? __fdiv_rn(am, 448.0f) : 1.0f;
+            uint32_t w = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (k < cnt) w |= enc_e4m3(__fdiv_rn(mt[k], scm), SR, SR ? hash32((idx0 + (uint32_t)k) ^ S.s_m) : 0U) << (8 * k);
+            st4_b8(static_cast<uint8_t*>(S.m) + i0, 4, S.vec_ok, w);
+            if (lane == 0) S.m_scale[blk] = scm;
+        } else {
+            const uint32_t vc = ld4_b8(static_cast<const uint8_t*>(S.v) + i0, st ? st + C::OFF_V + e0 : nullptr, 4, S.vec_ok);
+            const float su = S.v_scale[blk];
+            float vt[4], ut[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float u = __fmul_rn(dec_e5m2((vc >> (8 * k)) & 0xffU), su);
+                vt[k] = __fmul_rn(u, u);
+            }
+            if (i0 + kGroup <= S.fused_end) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) p[k] = adamw_elem_sq<true>(p[k], g[k], mt[k], vt[k], ut[k], c);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    p[k] = i0 + k < S.fused_end ? adamw_elem_sq<true>(p[k], g[k], mt[k], vt[k], ut[k], c)
+                                                : adamw_elem_sq<false>(p[k], g[k], mt[k], vt[k], ut[k], c);
+            }
+            store_master4<PT, SR>(S, i0, cnt, p);
+            store_out4(S, i0, cnt, p);
+            float am = 0.0f, au = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                ut[k] = vt[k] > 0.0f ? ut[k] : 0.0f;    // sqrt(max(v, 0)); NaN -> 0
+                const float a = fabsf(mt[k]);
+                am = (k < cnt && a > am) ? a : am;
+                au = (k < cnt && ut[k] > au) ? ut[k] : au;
+            }
+            am = warp_max(am);
+            au = warp_max(au);
+            const float scm = am > 0.0f ? __fdiv_rn(am, 448.0f) : 1.0f;
+            const float scu = au > 0.0f ? __fdiv_rn(au, 57344.0f) : 1.0f;
+            uint32_t wm = 0, wv = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t idx = idx0 + (uint32_t)k;
+                if (k < cnt) {
+                    wm |= enc_e4m3(__fdiv_rn(mt[k], scm), SR, SR ? hash32(idx ^ S.s_m) : 0U) << (8 * k);
+                    wv |= enc_e5m2(__fdiv_rn(ut[k], scu), SR, SR ? hash32(idx ^ S.s_v) : 0U) << (8 * k);
+                }
+            }
+            st4_b8(static_cast<uint8_t*>(S.m) + i0, 4, S.vec_ok, wm);
+            st4_b8(static_cast<uint8_t*>(S.v) + i0, 4, S.vec_ok, wv);
+            if (lane == 0) { S.m_scale[blk] = scm; S.v_scale[blk] = scu; }
         }
-        return;
     }
+}
 
-    float vt[8];
-    uint32_t vc[8];
-    const float su = blk_ok ? S.v_scale[blk] : 1.0f;
-    ld8_u8(static_cast<const uint8_t*>(S.v) + i0, blk_ok ? 8 : 0, vec, vc);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) { const float u = __fmul_rn(dec_e5m2(vc[k]), su); vt[k] = __fmul_rn(u, u); }
-    if (i0 + kVec <= S.fused_end) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = adamw_elem<true>(p[k], g[k], mt[k], vt[k], c);
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = adamw_elem_sel(p[k], g[k], mt[k], vt[k], c, i0 + k < S.fused_end);
-    }
-    st8_master<PT>(S, i0, cnt, vec, p);
-    st8_out(S, i0, cnt, vec, p);
-    float am = 0.0f, au = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const float u = __fsqrt_rn(vt[k] > 0.0f ? vt[k] : 0.0f);
-        vt[k] = u;
-        const float a = fabsf(mt[k]);
-        am = (k < cnt && a > am) ? a : am;
-        au = (k < cnt && u > au) ? u : au;
-    }
-    am = block_max16(am);
-    au = block_max16(au);
-    const float scm = am > 0.0f ? __fdiv_rn(am, 448.0f) : 1.0f;
-    const float scu = au > 0.0f ? __fdiv_rn(au, 57344.0f) : 1.0f;
-    if (blk_ok) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t idx = idx0 + (uint32_t)k;
-            mc[k] = k < cnt ? enc_e4m3(__fdiv_rn(mt[k], scm), sr, sr ? hash32(idx ^ S.s_m) : 0U) : 0U;
-            vc[k] = k < cnt ? enc_e5m2(__fdiv_rn(vt[k], scu), sr, sr ? hash32(idx ^ S.s_v) : 0U) : 0U;
-        }
-        st8_u8(static_cast<uint8_t*>(S.m) + i0, 8, vec, mc);
-        st8_u8(static_cast<uint8_t*>(S.v) + i0, 8, vec, vc);
-        if (lane16 == 0) { S.m_scale[blk] = scm; S.v_scale[blk] = scu; }
-    }
+template <int ALGO, int MV, int PT, int GT, bool SR>
+__device__ __forceinline__ void tile(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+{
+    if constexpr (MV == ABX_DT_FP8) tile_fp8<ALGO, PT, GT, SR>(S, base, st, gs);
+    else tile_dense<ALGO, MV, PT, GT, SR>(S, base, st, gs);
 }
 
 template <int NSEG>
@@ -408,18 +498,69 @@ __device__ __forceinline__ int find_segment(const KArgs<NSEG>& a, int64_t t)
     return lo;
 }
 
-template <int ALGO, int MV, int PT, int NSEG>
+// A tile streams through shared memory when it is whole and every streamed buffer is 16-byte aligned.
+__device__ __forceinline__ bool staged_tile(const KSeg& S, int64_t base) { return S.tma_ok && base + kTile <= S.n; }
+
+template <int ALGO, int MV, int PT, int GT, int NSEG>
 __global__ void __launch_bounds__(kThreads) update_kernel(const __grid_constant__ KArgs<NSEG> a)
 {
-    for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x) {
-        const KSeg& S = a.seg[find_segment(a, t)];
-        const int64_t base = (t - S.tile_begin) * kTile;
-        const int64_t i0 = base + threadIdx.x * kVec;
-        if constexpr (MV == ABX_DT_FP8) {
-            if (base + (threadIdx.x & ~31) * kVec < S.n) update8_fp8<ALGO, PT>(S, i0, a.g_scale);
-        } else {
-            update8_dense<ALGO, MV, PT>(S, i0, a.g_scale);
+    using C = Cfg<ALGO, MV, PT, GT>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = a.stages;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + S;
+    uint8_t* ring = smem + 128 * ((16 * S + 127) / 128);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
         }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---- producer: one lane streams tiles into the ring ----
+        if (lane != 0) return;
+        int k = 0;
+        for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
+            const int s = k % S;
+            if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
+            const KSeg& Sg = a.seg[find_segment(a, t)];
+            const int64_t base = (t - Sg.tile_begin) * kTile;
+            if (staged_tile(Sg, base)) {
+                uint8_t* st = ring + s * C::STAGE;
+                mbar_arrive_expect_tx(&full[s], C::STAGE);
+                bulk_load(st + C::OFF_P, static_cast<const char*>(Sg.p) + base * C::PB, kTile * C::PB, &full[s]);
+                if constexpr (C::LB > 0) bulk_load(st + C::OFF_L, Sg.p_lo + base, kTile, &full[s]);
+                bulk_load(st + C::OFF_G, static_cast<const char*>(Sg.g) + base * C::GB, kTile * C::GB, &full[s]);
+                bulk_load(st + C::OFF_M, static_cast<const char*>(Sg.m) + base * C::MB, kTile * C::MB, &full[s]);
+                if constexpr (C::VB > 0)
+                    bulk_load(st + C::OFF_V, static_cast<const char*>(Sg.v) + base * C::VB, kTile * C::VB, &full[s]);
+            } else {
+                mbar_arrive(&full[s]);   // consumers read this tile from global memory
+            }
+        }
+        // never leave with bulk copies in flight into this CTA's shared memory
+        for (int j = k - S < 0 ? 0 : k - S; j < k; ++j) mbar_wait(&full[j % S], (j / S) & 1);
+        return;
+    }
+
+    // ---- consumers ----
+    const float* gs = a.g_scale;
+    int k = 0;
+    for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
+        const int s = k % S;
+        if (!mbar_wait(&full[s], (k / S) & 1)) return;
+        const KSeg& Sg = a.seg[find_segment(a, t)];
+        const int64_t base = (t - Sg.tile_begin) * kTile;
+        const uint8_t* st = staged_tile(Sg, base) ? ring + s * C::STAGE : nullptr;
+        if (Sg.sr) tile<ALGO, MV, PT, GT, true>(Sg, base, st, gs);
+        else tile<ALGO, MV, PT, GT, false>(Sg, base, st, gs);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
 }
 
@@ -445,39 +586,54 @@ int lanes_of(int level)
     }
 }
 
-// Kernel table: index = ((algo * 3) + mv_index) * 2 + f24, mv_index 0/1/2 = F32/BF16/FP8.
-constexpr int kKinds = 12;
-using LaunchOne = cudaError_t (*)(const KArgs<1>&, int, cudaStream_t);
-using LaunchMany = cudaError_t (*)(const KArgs<kMaxSegs>&, int, cudaStream_t);
+// Kernel kinds: index = (((algo * 3 + mv) * 2 + f24) * 2 + bf16 grad), mv 0/1/2 = F32/BF16/FP8.
+constexpr int kKinds = 24;
+using LaunchOne = cudaError_t (*)(const KArgs<1>&, int, size_t, cudaStream_t);
+using LaunchMany = cudaError_t (*)(const KArgs<kMaxSegs>&, int, size_t, cudaStream_t);
 
-template <int A, int M, int P, int N>
-cudaError_t launch(const KArgs<N>& a, int grid, cudaStream_t st)
+template <int A, int M, int P, int G, int N>
+cudaError_t launch(const KArgs<N>& a, int grid, size_t smem, cudaStream_t st)
 {
-    update_kernel<A, M, P, N><<<grid, kThreads, 0, st>>>(a);
+    update_kernel<A, M, P, G, N><<<grid, kThreads, smem, st>>>(a);
     return cudaGetLastError();
 }
 
-template <int N>
-const void* kernel_ptr(int kind);
+#define ABX_FOR_KINDS(X, N)                                                                                   \
+    X(0, ABX_DT_F32, ABX_DT_F32, ABX_DT_F32, N), X(0, ABX_DT_F32, ABX_DT_F32, ABX_DT_BF16, N),                 \
+    X(0, ABX_DT_F32, ABX_DT_F24, ABX_DT_F32, N), X(0, ABX_DT_F32, ABX_DT_F24, ABX_DT_BF16, N),                 \
+    X(0, ABX_DT_BF16, ABX_DT_F32, ABX_DT_F32, N), X(0, ABX_DT_BF16, ABX_DT_F32, ABX_DT_BF16, N),               \
+    X(0, ABX_DT_BF16, ABX_DT_F24, ABX_DT_F32, N), X(0, ABX_DT_BF16, ABX_DT_F24, ABX_DT_BF16, N),               \
+    X(0, ABX_DT_FP8, ABX_DT_F32, ABX_DT_F32, N), X(0, ABX_DT_FP8, ABX_DT_F32, ABX_DT_BF16, N),                 \
+    X(0, ABX_DT_FP8, ABX_DT_F24, ABX_DT_F32, N), X(0, ABX_DT_FP8, ABX_DT_F24, ABX_DT_BF16, N),                 \
+    X(1, ABX_DT_F32, ABX_DT_F32, ABX_DT_F32, N), X(1, ABX_DT_F32, ABX_DT_F32, ABX_DT_BF16, N),                 \
+    X(1, ABX_DT_F32, ABX_DT_F24, ABX_DT_F32, N), X(1, ABX_DT_F32, ABX_DT_F24, ABX_DT_BF16, N),                 \
+    X(1, ABX_DT_BF16, ABX_DT_F32, ABX_DT_F32, N), X(1, ABX_DT_BF16, ABX_DT_F32, ABX_DT_BF16, N),               \
+    X(1, ABX_DT_BF16, ABX_DT_F24, ABX_DT_F32, N), X(1, ABX_DT_BF16, ABX_DT_F24, ABX_DT_BF16, N),               \
+    X(1, ABX_DT_FP8, ABX_DT_F32, ABX_DT_F32, N), X(1, ABX_DT_FP8, ABX_DT_F32, ABX_DT_BF16, N),                 \
+    X(1, ABX_DT_FP8, ABX_DT_F24, ABX_DT_F32, N), X(1, ABX_DT_FP8, ABX_DT_F24, ABX_DT_BF16, N)
 
-#define ABX_KIND_LIST(N)                                                                                  \
-    {(const void*)update_kernel<0, ABX_DT_F32, ABX_DT_F32, N>, (const void*)update_kernel<0, ABX_DT_F32, ABX_DT_F24, N>, \
-     (const void*)update_kernel<0, ABX_DT_BF16, ABX_DT_F32, N>, (const void*)update_kernel<0, ABX_DT_BF16, ABX_DT_F24, N>, \
-     (const void*)update_kernel<0, ABX_DT_FP8, ABX_DT_F32, N>, (const void*)update_kernel<0, ABX_DT_FP8, ABX_DT_F24, N>, \
-     (const void*)update_kernel<1, ABX_DT_F32, ABX_DT_F32, N>, (const void*)update_kernel<1, ABX_DT_F32, ABX_DT_F24, N>, \
-     (const void*)update_kernel<1, ABX_DT_BF16, ABX_DT_F32, N>, (const void*)update_kernel<1, ABX_DT_BF16, ABX_DT_F24, N>, \
-     (const void*)update_kernel<1, ABX_DT_FP8, ABX_DT_F32, N>, (const void*)update_kernel<1, ABX_DT_FP8, ABX_DT_F24, N>}
+#define ABX_KERNEL_PTR(A, M, P, G, N) (const void*)update_kernel<A, M, P, G, N>
+#define ABX_LAUNCH_PTR(A, M, P, G, N) launch<A, M, P, G, N>
+#define ABX_STAGE(A, M, P, G, N) Cfg<A, M, P, G>::STAGE
 
-#define ABX_LAUNCH_LIST(N)                                                                                         \
-    {launch<0, ABX_DT_F32, ABX_DT_F32, N>, launch<0, ABX_DT_F32, ABX_DT_F24, N>, launch<0, ABX_DT_BF16, ABX_DT_F32, N>, \
-     launch<0, ABX_DT_BF16, ABX_DT_F24, N>, launch<0, ABX_DT_FP8, ABX_DT_F32, N>, launch<0, ABX_DT_FP8, ABX_DT_F24, N>,  \
-     launch<1, ABX_DT_F32, ABX_DT_F32, N>, launch<1, ABX_DT_F32, ABX_DT_F24, N>, launch<1, ABX_DT_BF16, ABX_DT_F32, N>,   \
-     launch<1, ABX_DT_BF16, ABX_DT_F24, N>, launch<1, ABX_DT_FP8, ABX_DT_F32, N>, launch<1, ABX_DT_FP8, ABX_DT_F24, N>}
+const void* const kKernelsOne[kKinds] = {ABX_FOR_KINDS(ABX_KERNEL_PTR, 1)};
+const void* const kKernelsMany[kKinds] = {ABX_FOR_KINDS(ABX_KERNEL_PTR, kMaxSegs)};
+const LaunchOne kLaunchOne[kKinds] = {ABX_FOR_KINDS(ABX_LAUNCH_PTR, 1)};
+const LaunchMany kLaunchMany[kKinds] = {ABX_FOR_KINDS(ABX_LAUNCH_PTR, kMaxSegs)};
+const int kStageBytes[kKinds] = {ABX_FOR_KINDS(ABX_STAGE, 0)};
 
-const void* const kKernelsOne[kKinds] = ABX_KIND_LIST(1);
-const void* const kKernelsMany[kKinds] = ABX_KIND_LIST(kMaxSegs);
-const LaunchOne kLaunchOne[kKinds] = ABX_LAUNCH_LIST(1);
-const LaunchMany kLaunchMany[kKinds] = ABX_LAUNCH_LIST(kMaxSegs);
+// Ring geometry of a kind: stages and dynamic shared memory (barriers first, then the 128-aligned ring).
+int stages_of(int kind)
+{
+    const int s = kSmemTarget / kStageBytes[kind];
+    return s < 2 ? 2 : (s > 8 ? 8 : s);
+}
+
+size_t smem_of(int kind)
+{
+    const int s = stages_of(kind);
+    return (size_t)(128 * ((16 * s + 127) / 128) + s * kStageBytes[kind]);
+}
 
 // Per-device launch geometry: SM count and resident CTAs per SM of each kernel.
 constexpr int kMaxDevices = 64;
@@ -500,17 +656,20 @@ DeviceInfo* device_info(int* rc)
     std::call_once(d.once, [&d, dev] {
         cudaError_t err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
         for (int k = 0; k < kKinds && err == cudaSuccess; ++k) {
-            err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_one[k], kKernelsOne[k], kThreads, 0);
+            const int smem = (int)smem_of(k);
+            err = cudaFuncSetAttribute(kKernelsOne[k], cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (err == cudaSuccess)
-                err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_many[k], kKernelsMany[k], kThreads, 0);
+                err = cudaFuncSetAttribute(kKernelsMany[k], cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (err == cudaSuccess)
+                err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_one[k], kKernelsOne[k], kThreads, smem);
+            if (err == cudaSuccess)
+                err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.blocks_many[k], kKernelsMany[k], kThreads, smem);
         }
         d.err = err;
     });
     if (d.err != cudaSuccess) { *rc = set_error("querying the device", d.err); return nullptr; }
     return &d;
 }
-
-uint32_t step_seed(uint64_t base, uint64_t index, int64_t step);
 
 // Same checks, order and codes as the reference's check_segment (csrc:1537-1553).
 int check_segment(const abx_segment* s, bool need_group)
@@ -533,9 +692,10 @@ int check_segment(const abx_segment* s, bool need_group)
 
 bool aligned(const void* p, uintptr_t a) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Device accesses need natural alignment (the reference's host loads do not);
-// vector access additionally needs 16-byte (8-byte for byte arrays) alignment.
-int check_alignment(const abx_segment* s, bool* vec_ok)
+// Device accesses need natural alignment (the reference's host loads do not).  A segment whose buffers
+// allow 4-element vectors takes vector accesses on the direct path; one whose streamed buffers are all
+// 16-byte aligned has its whole tiles bulk-copied.
+int check_alignment(const abx_segment* s, bool* vec_ok, bool* tma_ok)
 {
     const bool lion = s->algorithm == ABX_ALGO_LION;
     const bool f24 = s->p_dtype == ABX_DT_F24;
@@ -544,15 +704,17 @@ int check_alignment(const abx_segment* s, bool* vec_ok)
     const uintptr_t oe = s->out_dtype == ABX_DT_F32 ? 4 : 2;
     const void* out = s->out_dtype != ABX_DT_NONE ? s->out : nullptr;
     const void* v = lion ? nullptr : s->v;
+    const uint8_t* lo = f24 ? s->p_lo : nullptr;
     const bool fp8 = s->mv_dtype == ABX_DT_FP8;
     if (!aligned(s->p, pe) || !aligned(s->g, ge) || !aligned(s->m, me) || !aligned(v, me) || !aligned(out, oe) ||
         (fp8 && (!aligned(s->m_scale, 4) || (!lion && !aligned(s->v_scale, 4))))) {
         snprintf(g_err, sizeof g_err, "segment buffer not aligned to its element size");
         return ABX_E_ALIGN;
     }
-    const uintptr_t mv = fp8 ? 8 : 16;
-    *vec_ok = aligned(s->p, 16) && aligned(f24 ? s->p_lo : nullptr, 8) && aligned(s->g, 16) && aligned(s->m, mv) &&
-              aligned(v, mv) && aligned(out, 16);
+    *vec_ok = aligned(s->p, 4 * pe) && aligned(lo, 4) && aligned(s->g, 4 * ge) && aligned(s->m, 4 * me) &&
+              aligned(v, 4 * me) && aligned(out, 4 * oe);
+    *tma_ok = *vec_ok && aligned(s->p, 16) && aligned(lo, 16) && aligned(s->g, 16) && aligned(s->m, 16) &&
+              aligned(v, 16);
     return ABX_OK;
 }
 
@@ -563,7 +725,8 @@ uint32_t hash32_host(uint32_t x)
     return x ^ (x >> 16);
 }
 
-void fill_kseg(KSeg& k, const abx_segment* s, const abx_hparams* h, int lanes, bool vec_ok, int64_t tile_begin)
+void fill_kseg(KSeg& k, const abx_segment* s, const abx_hparams* h, int lanes, bool vec_ok, bool tma_ok,
+               int64_t tile_begin)
 {
     const bool lion = s->algorithm == ABX_ALGO_LION;
     k.g = s->g;
@@ -582,16 +745,17 @@ void fill_kseg(KSeg& k, const abx_segment* s, const abx_hparams* h, int lanes, b
     k.s_v = hash32_host(h->seed ^ 0xA511E9B3U);
     k.s_p = hash32_host(h->seed ^ 0x6C8E9CF5U);
     k.off32 = (uint32_t)(uint64_t)s->offset;
-    k.g_dt = s->g_dtype;
     k.out_dt = s->out_dtype;
     k.sr = h->stochastic != 0;
     k.vec_ok = vec_ok ? 1 : 0;
+    k.tma_ok = tma_ok ? 1 : 0;
 }
 
 int kind_of(const abx_segment* s)
 {
     const int mv = s->mv_dtype == ABX_DT_F32 ? 0 : (s->mv_dtype == ABX_DT_BF16 ? 1 : 2);
-    return ((s->algorithm == ABX_ALGO_LION ? 1 : 0) * 3 + mv) * 2 + (s->p_dtype == ABX_DT_F24 ? 1 : 0);
+    return (((s->algorithm == ABX_ALGO_LION ? 1 : 0) * 3 + mv) * 2 + (s->p_dtype == ABX_DT_F24 ? 1 : 0)) * 2 +
+           (s->g_dtype == ABX_DT_BF16 ? 1 : 0);
 }
 
 int64_t tiles_of(int64_t n) { return (n + kTile - 1) / kTile; }
@@ -610,17 +774,18 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
     if (nsegs <= 0) return ABX_OK;
     if (!segs) return ABX_E_ARG;
     const bool from_groups = hps == nullptr;
-    std::vector<char> vec_ok(nsegs);
+    std::vector<char> vec_ok(nsegs), tma_ok(nsegs);
     for (int32_t i = 0; i < nsegs; ++i) {
         const int rc = check_segment(segs[i], from_groups);
         if (rc) return rc;
     }
     for (int32_t i = 0; i < nsegs; ++i) {
         if (segs[i]->n == 0) continue;
-        bool ok = false;
-        const int rc = check_alignment(segs[i], &ok);
+        bool vo = false, to = false;
+        const int rc = check_alignment(segs[i], &vo, &to);
         if (rc) return rc;
-        vec_ok[i] = ok;
+        vec_ok[i] = vo;
+        tma_ok[i] = to;
     }
     std::vector<abx_hparams> derived;
     if (from_groups) {
@@ -641,6 +806,7 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
         order.clear();
         for (int32_t i = 0; i < nsegs; ++i)
             if (segs[i]->n > 0 && kind_of(segs[i]) == kind) order.push_back(i);
+        const size_t smem = smem_of(kind);
         for (size_t b = 0; b < order.size(); b += kMaxSegs) {
             const int cnt = (int)(order.size() - b < (size_t)kMaxSegs ? order.size() - b : kMaxSegs);
             cudaError_t e;
@@ -648,24 +814,26 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
                 KArgs<1> a;
                 std::memset(&a, 0, sizeof a);
                 const int32_t i = order[b];
-                fill_kseg(a.seg[0], segs[i], &hps[i], lanes, vec_ok[i], 0);
+                fill_kseg(a.seg[0], segs[i], &hps[i], lanes, vec_ok[i], tma_ok[i], 0);
                 a.nseg = 1;
+                a.stages = stages_of(kind);
                 a.total_tiles = tiles_of(segs[i]->n);
                 a.g_scale = g_scale;
-                e = kLaunchOne[kind](a, grid_for(a.total_tiles, dev->blocks_one[kind], dev->sms, max_ctas), st);
+                e = kLaunchOne[kind](a, grid_for(a.total_tiles, dev->blocks_one[kind], dev->sms, max_ctas), smem, st);
             } else {
-                static thread_local KArgs<kMaxSegs> a;   // ~9.8 KB: kept off the stack
+                static thread_local KArgs<kMaxSegs> a;   // ~10 KB: kept off the stack
                 std::memset(&a, 0, sizeof a);
                 int64_t tiles = 0;
                 for (int j = 0; j < cnt; ++j) {
                     const int32_t i = order[b + j];
-                    fill_kseg(a.seg[j], segs[i], &hps[i], lanes, vec_ok[i], tiles);
+                    fill_kseg(a.seg[j], segs[i], &hps[i], lanes, vec_ok[i], tma_ok[i], tiles);
                     tiles += tiles_of(segs[i]->n);
                 }
                 a.nseg = cnt;
+                a.stages = stages_of(kind);
                 a.total_tiles = tiles;
                 a.g_scale = g_scale;
-                e = kLaunchMany[kind](a, grid_for(tiles, dev->blocks_many[kind], dev->sms, max_ctas), st);
+                e = kLaunchMany[kind](a, grid_for(tiles, dev->blocks_many[kind], dev->sms, max_ctas), smem, st);
             }
             if (e != cudaSuccess) return set_error("kernel launch", e);
             g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -794,3 +962,14 @@ ABX_API int abx_fused_adamw(float* p, const void* g, int g_dtype, void* m, void*
 ABX_API uint64_t abx_launch_count(void) { return abx::g_launches.load(); }
 
 ABX_API const char* abx_last_error(void) { return abx::g_err; }
+
+// Nonzero when a kernel's pipeline wait gave up since the last call (then reset).  Synchronizes the
+// current device; a correct pipeline never sets it.
+ABX_API int abx_pipeline_status(void)
+{
+    unsigned int v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, abx::g_pipeline_status, sizeof v);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(abx::g_pipeline_status, &zero, sizeof zero);
+    if (e != cudaSuccess) return abx::set_error("reading the pipeline status", e);
+    return (int)v;
+}

@@ -139,6 +139,7 @@ class UpdateEngine:
         self.algorithm = algorithm
         self.lion = algorithm == "lion"
         self.delay = False
+        self.may_delay = False   # delayed updates will be switched on (the optimizer sets this before any update)
         self.precision = precision
         self.master_precision = master_precision
         self.stochastic = stochastic_rounding
@@ -190,7 +191,10 @@ class UpdateEngine:
             if p.dtype not in _OUT_DTYPES:
                 raise TypeError(f"parameters must be float32 or bfloat16, got {p.dtype}")
             with torch.cuda.device(p.device):
-                if p.dtype == torch.float32 and self.master_precision == "fp32":
+                # An FP32 parameter is its own FP32 master -- unless its update must land somewhere else first
+                # (delayed updates, deferred write-back), which needs a master separate from the parameter.
+                if (p.dtype == torch.float32 and self.master_precision == "fp32" and not self.may_delay
+                        and self.overlap_writeback):
                     slot.master, slot.in_place = FP32Store.wrap(p.data.view(-1)), True
                 else:
                     slot.master = make_master(self.master_precision, slot.numel, init=p.detach(), device=p.device)

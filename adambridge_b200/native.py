@@ -205,6 +205,7 @@ class NativeKernels:
         lib.abx_step_seed.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64]
         lib.abx_last_error.restype = ctypes.c_char_p
         lib.abx_launch_count.restype = ctypes.c_uint64
+        lib.abx_pipeline_status.restype = ctypes.c_int
         self._lib = lib
 
     # -- rounding pattern ----------------------------------------------------
@@ -277,6 +278,14 @@ class NativeKernels:
     def launch_count(self) -> int:
         """Kernel launches made by libabx in this process so far."""
         return self._lib.abx_launch_count()
+
+    def pipeline_status(self) -> int:
+        """Nonzero if an update kernel's bounded pipeline wait gave up since the last call (then cleared).
+        Synchronizes with the current device."""
+        rc = self._lib.abx_pipeline_status()
+        if rc < 0:
+            self._check(rc, "abx_pipeline_status")
+        return rc
 
     @staticmethod
     def make_hparams(c: StepCoefficients, seed: int, stochastic: bool) -> _HParams:

@@ -127,6 +127,7 @@ class AdamBridge(torch.optim.Optimizer):
             transfer_buffer_bytes=None if transfer_buffer_mb is None else transfer_buffer_mb << 20,
             master_precision=self.master_precision, max_ctas=max_ctas)
         self._engine.delay = delay_updates and delay_warmup_steps == 0
+        self._engine.may_delay = delay_updates
         self._finalizer = weakref.finalize(self, UpdateEngine.close, self._engine)
         self._small_groups = self._build_small_groups()
 

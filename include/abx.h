@@ -178,6 +178,13 @@ int abx_fused_adamw(float* p, const void* g, int g_dtype, void* m, void* v, int 
 /* Kernel launches this library has made in this process, all threads and devices. */
 uint64_t abx_launch_count(void);
 
+/* The update kernels stream tiles through shared memory behind mbarrier waits,
+ * each bounded: a wait that gives up (never in correct operation) makes its CTA
+ * drain its copies and exit, and sets a status word on the device.  Returns that
+ * word for the current device (nonzero: some update since the last call is
+ * incomplete) and clears it, or ABX_E_CUDA.  Synchronizes with the device. */
+int abx_pipeline_status(void);
+
 /* Message of the last ABX_E_CUDA / ABX_E_ALIGN error on this thread (never NULL). */
 const char* abx_last_error(void);
 

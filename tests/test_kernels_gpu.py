@@ -234,3 +234,8 @@ def test_fp8_specials(kernels, oracle):
         a, b = got.buffers[k], ref.buffers[k]
         same = (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
         assert same.all(), (k, np.flatnonzero(~same)[:10])
+
+
+def test_pipeline_status_clear_after_all_updates(kernels):
+    """No bounded pipeline wait gave up in any update of this session (the status word is still zero)."""
+    assert kernels.pipeline_status() == 0
