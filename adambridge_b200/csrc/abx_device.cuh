@@ -15,6 +15,11 @@
 
 namespace abx {
 
+// The per-step coefficients of one segment (abx_hparams without the seed).
+struct Coef {
+    float b1, b2, omb1, omb2, decay, step, isbc2, eps;
+};
+
 __device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
@@ -100,11 +105,199 @@ __device__ __forceinline__ uint32_t enc_fp8(float x, bool sr, uint32_t r, float 
 __device__ __forceinline__ uint32_t enc_e4m3(float x, bool sr, uint32_t r) { return enc_fp8<3, 7>(x, sr, r, 448.0f, 0x7fU); }
 __device__ __forceinline__ uint32_t enc_e5m2(float x, bool sr, uint32_t r) { return enc_fp8<2, 15>(x, sr, r, 57344.0f, 0x7eU); }
 
-// ---- update arithmetic -------------------------------------------------------------
+// ---- FP8 codec on the hardware converters, 2 or 4 elements at a time ------------------
+// Decoding: the e4m3 / e5m2 -> f16 conversions and f16 -> f32 are exact for every finite
+// code, so they equal the reference's table lookups (NaN codes give a NaN).
+// Encoding: after the stochastic truncation of the fp32 significand (the reference's first
+// step), cvt.rn.satfinite rounds |x| to nearest even in the format and saturates at its
+// largest finite value -- what the reference's normal and subnormal branches compute -- for
+// every non-NaN input; a NaN input takes the reference's NaN code.  The sign is reattached
+// from x, so -0 keeps its sign as in the reference.
 
-struct Coef {
-    float b1, b2, omb1, omb2, decay, step, isbc2, eps;
+// 4 codes (byte k = element k) -> 4 floats.
+template <bool E4M3>
+__device__ __forceinline__ void dec4_fp8(uint32_t w, float (&x)[4])
+{
+    uint32_t h01, h23;
+    if (E4M3)
+        asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo; cvt.rn.f16x2.e4m3x2 %1, hi; }"
+            : "=r"(h01), "=r"(h23) : "r"(w));
+    else
+        asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e5m2x2 %0, lo; cvt.rn.f16x2.e5m2x2 %1, hi; }"
+            : "=r"(h01), "=r"(h23) : "r"(w));
+    asm("{ .reg .b16 a, b; mov.b32 {a, b}, %2; cvt.f32.f16 %0, a; cvt.f32.f16 %1, b; }" : "=f"(x[0]), "=f"(x[1]) : "r"(h01));
+    asm("{ .reg .b16 a, b; mov.b32 {a, b}, %2; cvt.f32.f16 %0, a; cvt.f32.f16 %1, b; }" : "=f"(x[2]), "=f"(x[3]) : "r"(h23));
+}
+
+// The reference's stochastic truncation of x's significand to MBITS bits, then |.|.
+template <int MBITS, bool SR>
+__device__ __forceinline__ float fp8_trunc_abs(float x, uint32_t r)
+{
+    constexpr uint32_t low = (1U << (23 - MBITS)) - 1U;
+    const uint32_t b = f2u(x);
+    const uint32_t t = SR ? ((b + (r & low)) & ~low) : b;
+    return u2f(t & 0x7fffffffU);
+}
+
+// Sign and NaN handling around a hardware code: sign | (NaN ? nan_code : code).
+__device__ __forceinline__ uint32_t fp8_finish(float x, uint32_t code, uint32_t nan_code)
+{
+    const uint32_t b = f2u(x);
+    return ((b >> 24) & 0x80U) | ((b & 0x7fffffffU) > 0x7f800000U ? nan_code : code);
+}
+
+// 4 floats -> 4 codes (byte k = element k); r[k] are the elements' random bits (SR only).
+template <bool E4M3, bool SR>
+__device__ __forceinline__ uint32_t enc4_fp8(const float (&x)[4], const uint32_t (&r)[4])
+{
+    constexpr int MB = E4M3 ? 3 : 2;
+    constexpr uint32_t NAN_CODE = E4M3 ? 0x7fU : 0x7eU;
+    float a[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) a[k] = fp8_trunc_abs<MB, SR>(x[k], r[k]);
+    uint16_t c01, c23;
+    if (E4M3) {
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(c01) : "f"(a[1]), "f"(a[0]));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(a[3]), "f"(a[2]));
+    } else {
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c01) : "f"(a[1]), "f"(a[0]));
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(a[3]), "f"(a[2]));
+    }
+    const uint32_t c[4] = {(uint32_t)c01 & 0xffU, (uint32_t)c01 >> 8, (uint32_t)c23 & 0xffU, (uint32_t)c23 >> 8};
+    return fp8_finish(x[0], c[0], NAN_CODE) | (fp8_finish(x[1], c[1], NAN_CODE) << 8) |
+           (fp8_finish(x[2], c[2], NAN_CODE) << 16) | (fp8_finish(x[3], c[3], NAN_CODE) << 24);
+}
+
+// ---- packed pairs: sm_100a f32x2 arithmetic ---------------------------------------------
+// fma/mul/add.rn.f32x2 round each lane exactly as the scalar instruction does, so a pair of
+// elements costs one FP32 instruction per operation instead of two.
+typedef unsigned long long f2x;
+
+__device__ __forceinline__ f2x pk2(float a, float b)
+{
+    f2x r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+__device__ __forceinline__ void up2(f2x r, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r)); }
+
+__device__ __forceinline__ f2x fma2(f2x a, f2x b, f2x c)
+{
+    f2x d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ f2x mul2(f2x a, f2x b)
+{
+    f2x d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// The update's coefficients as pairs (both lanes equal).
+struct Coef2 {
+    f2x b1, b2, omb1, omb2, decay, nstep, isbc2, eps;
 };
+
+__device__ __forceinline__ Coef2 coef2(const Coef& c)
+{
+    return Coef2{pk2(c.b1, c.b1), pk2(c.b2, c.b2), pk2(c.omb1, c.omb1), pk2(c.omb2, c.omb2),
+                 pk2(c.decay, c.decay), pk2(-c.step, -c.step), pk2(c.isbc2, c.isbc2), pk2(c.eps, c.eps)};
+}
+
+// Fused AdamW on elements (2j, 2j+1) -- the vector-loop arithmetic of adamw_elem<true>, pairwise.
+// (s0, s1) receive sqrt(new v).
+__device__ __forceinline__ void adamw2_fused(float& p0, float& p1, float g0, float g1, float& m0, float& m1,
+                                             float& v0, float& v1, const Coef2& c, float& s0, float& s1)
+{
+    const f2x G = pk2(g0, g1);
+    const f2x P = mul2(pk2(p0, p1), c.decay);
+    const f2x M = fma2(c.b1, pk2(m0, m1), mul2(c.omb1, G));
+    const f2x V = fma2(c.b2, pk2(v0, v1), mul2(c.omb2, mul2(G, G)));
+    up2(M, m0, m1);
+    up2(V, v0, v1);
+    s0 = __fsqrt_rn(v0);
+    s1 = __fsqrt_rn(v1);
+    float d0, d1;
+    up2(fma2(pk2(s0, s1), c.isbc2, c.eps), d0, d1);
+    up2(fma2(c.nstep, pk2(__fdiv_rn(m0, d0), __fdiv_rn(m1, d1)), P), p0, p1);
+}
+
+// Lion on elements (2j, 2j+1), pairwise.
+__device__ __forceinline__ void lion2(float& p0, float& p1, float g0, float g1, float& m0, float& m1,
+                                      const Coef2& c, float step)
+{
+    const f2x G = pk2(g0, g1);
+    const f2x Mo = pk2(m0, m1);
+    float c0, c1;
+    up2(fma2(c.b1, Mo, mul2(c.omb1, G)), c0, c1);
+    const float u0 = c0 > 0.0f ? step : (c0 < 0.0f ? -step : 0.0f);
+    const float u1 = c1 > 0.0f ? step : (c1 < 0.0f ? -step : 0.0f);
+    up2(fma2(pk2(p0, p1), c.decay, pk2(-u0, -u1)), p0, p1);
+    up2(fma2(c.b2, Mo, mul2(c.omb2, G)), m0, m1);
+}
+
+// Block scale absmax / fmax, correctly rounded: the constant reciprocal of fmax with Markstein's
+// correction (exact remainder for amax >= 2^-100), else IEEE division.  amax > 0.
+template <bool E4M3>
+__device__ __forceinline__ float scale_of(float amax)
+{
+    const float fmax = E4M3 ? 448.0f : 57344.0f;
+    const float y = E4M3 ? 0x1.24924ap-9f : 0x1.24924ap-16f;   // RN(1/448), RN(1/57344)
+    if (amax < 0x1p-100f) return __fdiv_rn(amax, fmax);
+    const float q0 = __fmul_rn(amax, y);
+    return __fmaf_rn(__fmaf_rn(-q0, fmax, amax), y, q0);
+}
+
+// 4 floats -> 4 codes with the sign handled by the converter: the stochastic truncation only touches
+// significand bits (a carry out of them ends at the exponent, never in the sign bit, for any non-NaN
+// value), and cvt.rn.satfinite is symmetric in the sign, so sign | code(|t|) == cvt(t).  A NaN
+// input (rare) falls back to enc4_fp8, which gives the reference's NaN code.
+template <bool E4M3, bool SR>
+__device__ __forceinline__ uint32_t enc4_signed(const float (&x)[4], const uint32_t (&r)[4])
+{
+    constexpr uint32_t low = (1U << (23 - (E4M3 ? 3 : 2))) - 1U;
+    float a[4];
+    bool nan = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t b = f2u(x[k]);
+        a[k] = u2f(SR ? ((b + (r[k] & low)) & ~low) : b);
+        nan |= (b & 0x7fffffffU) > 0x7f800000U;
+    }
+    uint16_t c01, c23;
+    if (E4M3) {
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(c01) : "f"(a[1]), "f"(a[0]));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(a[3]), "f"(a[2]));
+    } else {
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c01) : "f"(a[1]), "f"(a[0]));
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(a[3]), "f"(a[2]));
+    }
+    const uint32_t w = (uint32_t)c01 | ((uint32_t)c23 << 16);
+    return nan ? enc4_fp8<E4M3, SR>(x, r) : w;
+}
+
+// ---- division by a block scale -------------------------------------------------------
+// x / s, correctly rounded, for a block-constant s > 0: with y = RN(1/s), q0 = RN(|x| y) is within
+// one ulp of |x|/s, the remainder |x| - s q0 is exact in one FMA, and RN(q0 + remainder * y) is the
+// correctly rounded quotient (P. Markstein, IBM J. Res. Dev. 34(1), 1990; the correction theorem
+// for division).  Exactness of the remainder needs its quantum above the subnormal range: it holds
+// for |x| >= 2^-100, and below that the quotient (|x| / s < 2^-20 when s >= 2^-80) encodes to a
+// zero code whatever its last bits.  `fast_scale` tells whether s is in that range; otherwise the
+// caller divides with __fdiv_rn.
+__device__ __forceinline__ bool fast_scale(float s) { return s >= 0x1p-80f && s <= 0x1p100f; }
+
+__device__ __forceinline__ float div_by_scale(float x, float s, float y)
+{
+    const float a = fabsf(x);
+    const float q0 = __fmul_rn(a, y);
+    const float q = __fmaf_rn(__fmaf_rn(-q0, s, a), y, q0);
+    return copysignf(q, x);
+}
+
+// ---- update arithmetic -------------------------------------------------------------
 
 // AdamW on one element in torch.optim.AdamW's order; m and v updated in fp32.
 // Returns the new master value before storage rounding.

@@ -101,7 +101,21 @@ struct Cfg {
     static constexpr int OFF_G = OFF_L + kTile * LB;
     static constexpr int OFF_M = OFF_G + kTile * GB;
     static constexpr int OFF_V = OFF_M + kTile * MB;
-    static constexpr int STAGE = OFF_V + kTile * VB;
+    static constexpr int ARR = OFF_V + kTile * VB;         // bytes of the element arrays
+    static constexpr bool FP8 = MV == ABX_DT_FP8;
+    // FP8: the tile's 16 block scales of m (and v), bulk-copied as the 16-byte-aligned window that holds
+    // them (64 or 80 bytes) into a 128-byte slot; consumers index it from the window's start.
+    static constexpr int OFF_SM = ARR;
+    static constexpr int OFF_SV = ARR + 128;
+    static constexpr int STAGE = ARR + (FP8 ? (VB > 0 ? 256 : 128) : 0);
+};
+
+// Per-stage description of the tile, written by the producer before it arrives on the stage's
+// full barrier (so consumers see it after their wait): which segment, where, whether staged.
+struct TileMeta {
+    int32_t seg;
+    int32_t staged;
+    int64_t base;
 };
 
 // ---- PTX: mbarriers and 1-D TMA bulk copies -----------------------------------------
@@ -391,6 +405,27 @@ __device__ __forceinline__ float warp_max(float x)
 
 // FP8 moments: in each half tile, warp w owns block w (128 elements, 4 per lane).  Called by whole
 // warps; a warp whose block starts past the end of the segment skips it (the test is warp-uniform).
+// Codes of 4 elements x[k] / s (zero for elements past the end, k >= cnt: the block padding), with the
+// random bits of stream `seed`.  s is the block's scale (warp-uniform, so the branch is too).
+template <bool E4M3, bool SR>
+__device__ __forceinline__ uint32_t encode4(const float (&x)[4], float s, int cnt, uint32_t idx0, uint32_t seed)
+{
+    float q[4];
+    if (fast_scale(s)) {
+        const float y = __frcp_rn(s);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = div_by_scale(x[k], s, y);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = __fdiv_rn(x[k], s);
+    }
+    uint32_t r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r[k] = SR ? hash32((idx0 + (uint32_t)k) ^ seed) : 0U;
+    const uint32_t w = enc4_fp8<E4M3, SR>(q, r);
+    return cnt >= 4 ? w : (cnt <= 0 ? 0U : w & (0xffffffffU >> (8 * (4 - cnt))));
+}
+
 template <int ALGO, int PT, int GT, bool SR>
 __device__ __forceinline__ void tile_fp8(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
 {
@@ -412,7 +447,9 @@ __device__ __forceinline__ void tile_fp8(const KSeg& S, int64_t base, const uint
         const float sm = S.m_scale[blk];
         float g[4], p[4], mt[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) mt[k] = __fmul_rn(dec_e4m3((mc >> (8 * k)) & 0xffU), sm);
+        dec4_fp8<true>(mc, mt);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mt[k] = __fmul_rn(mt[k], sm);
         grad4<GT>(S, i0, cnt, st ? st + C::OFF_G + e0 * C::GB : nullptr, gs, g);
         master4<PT>(S, i0, cnt, st ? st + C::OFF_P + e0 * C::PB : nullptr, st ? st + C::OFF_L + e0 : nullptr, p);
         if constexpr (ALGO == ABX_ALGO_LION) {
@@ -425,19 +462,16 @@ __device__ __forceinline__ void tile_fp8(const KSeg& S, int64_t base, const uint
             for (int k = 0; k < 4; ++k) { const float a = fabsf(mt[k]); am = (k < cnt && a > am) ? a : am; }
             am = warp_max(am);
             const float scm = am > 0.0f ? __fdiv_rn(am, 448.0f) : 1.0f;
-            uint32_t w = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                if (k < cnt) w |= enc_e4m3(__fdiv_rn(mt[k], scm), SR, SR ? hash32((idx0 + (uint32_t)k) ^ S.s_m) : 0U) << (8 * k);
-            st4_b8(static_cast<uint8_t*>(S.m) + i0, 4, S.vec_ok, w);
+            st4_b8(static_cast<uint8_t*>(S.m) + i0, 4, S.vec_ok, encode4<true, SR>(mt, scm, cnt, idx0, S.s_m));
             if (lane == 0) S.m_scale[blk] = scm;
         } else {
             const uint32_t vc = ld4_b8(static_cast<const uint8_t*>(S.v) + i0, st ? st + C::OFF_V + e0 : nullptr, 4, S.vec_ok);
             const float su = S.v_scale[blk];
             float vt[4], ut[4];
+            dec4_fp8<false>(vc, vt);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float u = __fmul_rn(dec_e5m2((vc >> (8 * k)) & 0xffU), su);
+                const float u = __fmul_rn(vt[k], su);
                 vt[k] = __fmul_rn(u, u);
             }
             if (i0 + kGroup <= S.fused_end) {
@@ -463,17 +497,8 @@ __device__ __forceinline__ void tile_fp8(const KSeg& S, int64_t base, const uint
             au = warp_max(au);
             const float scm = am > 0.0f ? __fdiv_rn(am, 448.0f) : 1.0f;
             const float scu = au > 0.0f ? __fdiv_rn(au, 57344.0f) : 1.0f;
-            uint32_t wm = 0, wv = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint32_t idx = idx0 + (uint32_t)k;
-                if (k < cnt) {
-                    wm |= enc_e4m3(__fdiv_rn(mt[k], scm), SR, SR ? hash32(idx ^ S.s_m) : 0U) << (8 * k);
-                    wv |= enc_e5m2(__fdiv_rn(ut[k], scu), SR, SR ? hash32(idx ^ S.s_v) : 0U) << (8 * k);
-                }
-            }
-            st4_b8(static_cast<uint8_t*>(S.m) + i0, 4, S.vec_ok, wm);
-            st4_b8(static_cast<uint8_t*>(S.v) + i0, 4, S.vec_ok, wv);
+            st4_b8(static_cast<uint8_t*>(S.m) + i0, 4, S.vec_ok, encode4<true, SR>(mt, scm, cnt, idx0, S.s_m));
+            st4_b8(static_cast<uint8_t*>(S.v) + i0, 4, S.vec_ok, encode4<false, SR>(ut, scu, cnt, idx0, S.s_v));
             if (lane == 0) { S.m_scale[blk] = scm; S.v_scale[blk] = scu; }
         }
     }
@@ -501,15 +526,226 @@ __device__ __forceinline__ int find_segment(const KArgs<NSEG>& a, int64_t t)
 // A tile streams through shared memory when it is whole and every streamed buffer is 16-byte aligned.
 __device__ __forceinline__ bool staged_tile(const KSeg& S, int64_t base) { return S.tma_ok && base + kTile <= S.n; }
 
+// ---- fast path: a whole tile staged in shared memory ------------------------------------
+// Every element is valid and every buffer aligned, so loads come from shared memory and stores go
+// straight to HBM as vectors, with no per-element masks or alignment branches.
+
+__device__ __forceinline__ void lds_f32x4(const uint8_t* s, float (&x)[4])
+{
+    const float4 a = *reinterpret_cast<const float4*>(s);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+}
+
+__device__ __forceinline__ void lds_b16x4(const uint8_t* s, float (&x)[4])
+{
+    const uint2 a = *reinterpret_cast<const uint2*>(s);
+    const uint32_t w[2] = {a.x, a.y};
+    unpack_b16(w, x);
+}
+
+template <int GT>
+__device__ __forceinline__ void fast_grad4(const uint8_t* s, const float* gs, float (&g)[4])
+{
+    if constexpr (GT == ABX_DT_BF16) lds_b16x4(s, g);
+    else lds_f32x4(s, g);
+    if (gs != nullptr) {
+        const float f = *gs;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            g[k] = __fmul_rn(g[k], f);
+            if constexpr (GT == ABX_DT_BF16) g[k] = u2f(bf16_rne(f2u(g[k])) & 0xffff0000U);
+        }
+    }
+}
+
+template <int PT>
+__device__ __forceinline__ void fast_master4(const uint8_t* sp, const uint8_t* sl, float (&p)[4])
+{
+    if constexpr (PT == ABX_DT_F24) {
+        const uint2 a = *reinterpret_cast<const uint2*>(sp);
+        const uint32_t lo = *reinterpret_cast<const uint32_t*>(sl);
+        p[0] = u2f((a.x << 16) | ((lo & 0xffU) << 8));
+        p[1] = u2f((a.x & 0xffff0000U) | (lo & 0xff00U));
+        p[2] = u2f((a.y << 16) | ((lo >> 8) & 0xff00U));
+        p[3] = u2f((a.y & 0xffff0000U) | ((lo >> 16) & 0xff00U));
+    } else {
+        lds_f32x4(sp, p);
+    }
+}
+
+template <int MV>
+__device__ __forceinline__ void fast_moment4(const uint8_t* s, float (&x)[4])
+{
+    if constexpr (MV == ABX_DT_BF16) lds_b16x4(s, x);
+    else lds_f32x4(s, x);
+}
+
+template <int ALGO, int MV, int PT, int GT, bool SR>
+__device__ __forceinline__ void fast_dense(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+{
+    using C = Cfg<ALGO, MV, PT, GT>;
+    const Coef c = S.c;
+    const Coef2 c2 = coef2(c);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e0 = h * kHalf + threadIdx.x * kGroup;
+        const int64_t i0 = base + e0;
+        const uint32_t idx0 = S.off32 + (uint32_t)i0;
+        float g[4], p[4], m[4];
+        fast_grad4<GT>(st + C::OFF_G + e0 * C::GB, gs, g);
+        fast_master4<PT>(st + C::OFF_P + e0 * C::PB, st + C::OFF_L + e0, p);
+        fast_moment4<MV>(st + C::OFF_M + e0 * C::MB, m);
+        if constexpr (ALGO == ABX_ALGO_LION) {
+            lion2(p[0], p[1], g[0], g[1], m[0], m[1], c2, c.step);
+            lion2(p[2], p[3], g[2], g[3], m[2], m[3], c2, c.step);
+            store_master4<PT, SR>(S, i0, 4, p);
+            store_moment4<MV, SR>(S.m, i0, 4, true, m, S.s_m, idx0);
+        } else {
+            float v[4];
+            fast_moment4<MV>(st + C::OFF_V + e0 * C::MB, v);
+            if (i0 + kGroup <= S.fused_end) {
+                float s0, s1, s2, s3;
+                adamw2_fused(p[0], p[1], g[0], g[1], m[0], m[1], v[0], v[1], c2, s0, s1);
+                adamw2_fused(p[2], p[3], g[2], g[3], m[2], m[3], v[2], v[3], c2, s2, s3);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) p[k] = adamw_elem_sel(p[k], g[k], m[k], v[k], c, i0 + k < S.fused_end);
+            }
+            store_master4<PT, SR>(S, i0, 4, p);
+            store_moment4<MV, SR>(S.m, i0, 4, true, m, S.s_m, idx0);
+            store_moment4<MV, SR>(S.v, i0, 4, true, v, S.s_v, idx0);
+        }
+        store_out4(S, i0, 4, p);
+    }
+}
+
+// Max over the warp of values >= 0 (never NaN): non-negative floats order like their bit patterns.
+__device__ __forceinline__ float warp_max_nonneg(float x)
+{
+    return u2f(__reduce_max_sync(0xffffffffU, f2u(x)));
+}
+
+__device__ __forceinline__ float absmax4(const float (&x)[4])
+{
+    // fmaxf drops a NaN operand, as the reference's "a > am ? a : am" skips it
+    return fmaxf(fmaxf(fmaxf(fmaxf(0.0f, fabsf(x[0])), fabsf(x[1])), fabsf(x[2])), fabsf(x[3]));
+}
+
+// Codes of x[k] / s for a whole group of 4 (fast path of encode4).
+template <bool E4M3, bool SR>
+__device__ __forceinline__ uint32_t fast_encode4(const float (&x)[4], float s, uint32_t idx0, uint32_t seed)
+{
+    float q[4];
+    if (fast_scale(s)) {
+        const float y = __frcp_rn(s);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = div_by_scale(x[k], s, y);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = __fdiv_rn(x[k], s);
+    }
+    uint32_t r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r[k] = SR ? hash32((idx0 + (uint32_t)k) ^ seed) : 0U;
+    return enc4_signed<E4M3, SR>(q, r);
+}
+
+template <int ALGO, int PT, int GT, bool SR>
+__device__ __forceinline__ void fast_fp8(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+{
+    using C = Cfg<ALGO, ABX_DT_FP8, PT, GT>;
+    const Coef c = S.c;
+    const Coef2 c2 = coef2(c);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t blk0 = base >> 7;   // first block of the tile
+    const float* swm = reinterpret_cast<const float*>(st + C::OFF_SM + (reinterpret_cast<uintptr_t>(S.m_scale + blk0) & 15));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e0 = h * kHalf + threadIdx.x * kGroup;
+        const int64_t i0 = base + e0;
+        const uint32_t idx0 = S.off32 + (uint32_t)i0;
+        const int bt = h * kConsumerWarps + warp;   // this warp's block within the tile
+        float g[4], p[4], mt[4];
+        const float sm = swm[bt];
+        dec4_fp8<true>(*reinterpret_cast<const uint32_t*>(st + C::OFF_M + e0), mt);
+        up2(mul2(pk2(mt[0], mt[1]), pk2(sm, sm)), mt[0], mt[1]);
+        up2(mul2(pk2(mt[2], mt[3]), pk2(sm, sm)), mt[2], mt[3]);
+        fast_grad4<GT>(st + C::OFF_G + e0 * C::GB, gs, g);
+        fast_master4<PT>(st + C::OFF_P + e0 * C::PB, st + C::OFF_L + e0, p);
+        if constexpr (ALGO == ABX_ALGO_LION) {
+            lion2(p[0], p[1], g[0], g[1], mt[0], mt[1], c2, c.step);
+            lion2(p[2], p[3], g[2], g[3], mt[2], mt[3], c2, c.step);
+            store_master4<PT, SR>(S, i0, 4, p);
+            store_out4(S, i0, 4, p);
+            const float am = warp_max_nonneg(absmax4(mt));
+            const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode4<true, SR>(mt, scm, idx0, S.s_m);
+            if (lane == 0) S.m_scale[blk0 + bt] = scm;
+        } else {
+            const float* swv = reinterpret_cast<const float*>(st + C::OFF_SV + (reinterpret_cast<uintptr_t>(S.v_scale + blk0) & 15));
+            const float su = swv[bt];
+            float vt[4], ut[4];
+            dec4_fp8<false>(*reinterpret_cast<const uint32_t*>(st + C::OFF_V + e0), vt);
+            {
+                const f2x SU = pk2(su, su);
+                const f2x U01 = mul2(pk2(vt[0], vt[1]), SU), U23 = mul2(pk2(vt[2], vt[3]), SU);
+                up2(mul2(U01, U01), vt[0], vt[1]);
+                up2(mul2(U23, U23), vt[2], vt[3]);
+            }
+            if (i0 + kGroup <= S.fused_end) {
+                adamw2_fused(p[0], p[1], g[0], g[1], mt[0], mt[1], vt[0], vt[1], c2, ut[0], ut[1]);
+                adamw2_fused(p[2], p[3], g[2], g[3], mt[2], mt[3], vt[2], vt[3], c2, ut[2], ut[3]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    p[k] = i0 + k < S.fused_end ? adamw_elem_sq<true>(p[k], g[k], mt[k], vt[k], ut[k], c)
+                                                : adamw_elem_sq<false>(p[k], g[k], mt[k], vt[k], ut[k], c);
+            }
+            store_master4<PT, SR>(S, i0, 4, p);
+            store_out4(S, i0, 4, p);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ut[k] = vt[k] > 0.0f ? ut[k] : 0.0f;   // sqrt(max(v, 0)); NaN -> 0
+            const float am = warp_max_nonneg(absmax4(mt));
+            const float au = warp_max_nonneg(fmaxf(fmaxf(ut[0], ut[1]), fmaxf(ut[2], ut[3])));
+            const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
+            const float scu = au > 0.0f ? scale_of<false>(au) : 1.0f;
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode4<true, SR>(mt, scm, idx0, S.s_m);
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.v) + i0) = fast_encode4<false, SR>(ut, scu, idx0, S.s_v);
+            if (lane == 0) { S.m_scale[blk0 + bt] = scm; S.v_scale[blk0 + bt] = scu; }
+        }
+    }
+}
+
+template <int ALGO, int MV, int PT, int GT, bool SR>
+__device__ __forceinline__ void fast_tile(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+{
+    if constexpr (MV == ABX_DT_FP8) fast_fp8<ALGO, PT, GT, SR>(S, base, st, gs);
+    else fast_dense<ALGO, MV, PT, GT, SR>(S, base, st, gs);
+}
+
+// The 16-byte-aligned window [floor16(p), ceil16(p + bytes)) around `bytes` valid bytes at p: the bulk
+// copy reads only 16-byte chunks that hold valid bytes.
+__device__ __forceinline__ uint32_t window_bytes(const void* p, uint32_t bytes)
+{
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    return (uint32_t)(((a + bytes + 15) & ~(uintptr_t)15) - (a & ~(uintptr_t)15));
+}
+
+__device__ __forceinline__ const void* window_start(const void* p)
+{
+    return reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)15);
+}
+
 template <int ALGO, int MV, int PT, int GT, int NSEG>
-__global__ void __launch_bounds__(kThreads) update_kernel(const __grid_constant__ KArgs<NSEG> a)
+__global__ void __launch_bounds__(kThreads, 3) update_kernel(const __grid_constant__ KArgs<NSEG> a)
 {
     using C = Cfg<ALGO, MV, PT, GT>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = a.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + S;
-    uint8_t* ring = smem + 128 * ((16 * S + 127) / 128);
+    TileMeta* meta = reinterpret_cast<TileMeta*>(empty + S);
+    uint8_t* ring = smem + 128 * ((32 * S + 127) / 128);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -522,23 +758,39 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const __grid_constant_
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-        // ---- producer: one lane streams tiles into the ring ----
+        // ---- producer: one lane describes each tile and streams staged ones into the ring ----
         if (lane != 0) return;
         int k = 0;
         for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
             const int s = k % S;
             if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
-            const KSeg& Sg = a.seg[find_segment(a, t)];
+            const int si = find_segment(a, t);
+            const KSeg& Sg = a.seg[si];
             const int64_t base = (t - Sg.tile_begin) * kTile;
-            if (staged_tile(Sg, base)) {
+            const bool staged = staged_tile(Sg, base);
+            meta[s].seg = si;
+            meta[s].staged = staged;
+            meta[s].base = base;
+            if (staged) {
                 uint8_t* st = ring + s * C::STAGE;
-                mbar_arrive_expect_tx(&full[s], C::STAGE);
+                uint32_t bytes = C::ARR;
+                uint32_t wm = 0, wv = 0;
+                if constexpr (C::FP8) {
+                    wm = window_bytes(Sg.m_scale + (base >> 7), 4 * (kTile / 128));
+                    if constexpr (C::VB > 0) wv = window_bytes(Sg.v_scale + (base >> 7), 4 * (kTile / 128));
+                    bytes += wm + wv;
+                }
+                mbar_arrive_expect_tx(&full[s], bytes);
                 bulk_load(st + C::OFF_P, static_cast<const char*>(Sg.p) + base * C::PB, kTile * C::PB, &full[s]);
                 if constexpr (C::LB > 0) bulk_load(st + C::OFF_L, Sg.p_lo + base, kTile, &full[s]);
                 bulk_load(st + C::OFF_G, static_cast<const char*>(Sg.g) + base * C::GB, kTile * C::GB, &full[s]);
                 bulk_load(st + C::OFF_M, static_cast<const char*>(Sg.m) + base * C::MB, kTile * C::MB, &full[s]);
                 if constexpr (C::VB > 0)
                     bulk_load(st + C::OFF_V, static_cast<const char*>(Sg.v) + base * C::VB, kTile * C::VB, &full[s]);
+                if constexpr (C::FP8) {
+                    bulk_load(st + C::OFF_SM, window_start(Sg.m_scale + (base >> 7)), wm, &full[s]);
+                    if constexpr (C::VB > 0) bulk_load(st + C::OFF_SV, window_start(Sg.v_scale + (base >> 7)), wv, &full[s]);
+                }
             } else {
                 mbar_arrive(&full[s]);   // consumers read this tile from global memory
             }
@@ -554,11 +806,16 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const __grid_constant_
     for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
         const int s = k % S;
         if (!mbar_wait(&full[s], (k / S) & 1)) return;
-        const KSeg& Sg = a.seg[find_segment(a, t)];
-        const int64_t base = (t - Sg.tile_begin) * kTile;
-        const uint8_t* st = staged_tile(Sg, base) ? ring + s * C::STAGE : nullptr;
-        if (Sg.sr) tile<ALGO, MV, PT, GT, true>(Sg, base, st, gs);
-        else tile<ALGO, MV, PT, GT, false>(Sg, base, st, gs);
+        const TileMeta tm = meta[s];
+        const KSeg& Sg = a.seg[tm.seg];
+        if (tm.staged) {
+            const uint8_t* st = ring + s * C::STAGE;
+            if (Sg.sr) fast_tile<ALGO, MV, PT, GT, true>(Sg, tm.base, st, gs);
+            else fast_tile<ALGO, MV, PT, GT, false>(Sg, tm.base, st, gs);
+        } else {
+            if (Sg.sr) tile<ALGO, MV, PT, GT, true>(Sg, tm.base, nullptr, gs);
+            else tile<ALGO, MV, PT, GT, false>(Sg, tm.base, nullptr, gs);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -632,7 +889,7 @@ int stages_of(int kind)
 size_t smem_of(int kind)
 {
     const int s = stages_of(kind);
-    return (size_t)(128 * ((16 * s + 127) / 128) + s * kStageBytes[kind]);
+    return (size_t)(128 * ((32 * s + 127) / 128) + s * kStageBytes[kind]);
 }
 
 // Per-device launch geometry: SM count and resident CTAs per SM of each kernel.

@@ -236,6 +236,38 @@ def test_fp8_specials(kernels, oracle):
         assert same.all(), (k, np.flatnonzero(~same)[:10])
 
 
+@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("sr", [1, 0])
+def test_fp8_codec_wide_dynamic_range(kernels, oracle, algo, sr):
+    """FP8 moments whose block scales span 1e-30 .. 1e10 and gradients spanning 1e-30 .. 1e3: blocks on both
+    sides of the reciprocal-division range, subnormal and saturated codes, every code value.  Bit-exact with the
+    oracle (which divides and encodes exactly as the reference does)."""
+    n = 1 << 20
+    hs = O.HostSegment.random(n, O.DT_F32, O.DT_FP8, O.DT_BF16, O.DT_F32, algo, seed=77)
+    rng = np.random.default_rng(78)
+    nb = hs.nblocks
+    hs.buffers["m"][:] = rng.integers(0, 256, hs.moment_len(), dtype=np.uint8)
+    hs.buffers["m"][(hs.buffers["m"] & 0x7F) == 0x7F] = 0x11          # no NaN codes in the starting state
+    hs.buffers["m_scale"][:] = np.exp(rng.uniform(np.log(1e-30), np.log(1e10), nb)).astype(np.float32)
+    if algo == O.ADAMW:
+        hs.buffers["v"][:] = rng.integers(0, 0x7C, hs.moment_len(), dtype=np.uint8)
+        hs.buffers["v_scale"][:] = np.exp(rng.uniform(np.log(1e-30), np.log(1e10), nb)).astype(np.float32)
+    kernels.set_simd_level("avx512")
+    dev = to_device(hs)
+    ref = hs.clone()
+    pg = product_group(**GROUP, stochastic=sr)
+    og = O.Group(**GROUP, stochastic=sr)
+    for step in (1, 2, 3):
+        g = (np.sign(rng.standard_normal(n)) * np.exp(rng.uniform(np.log(1e-30), np.log(1e3), n))).astype(np.float32)
+        ref.buffers["g"][:] = g
+        dev["g"].copy_(torch.from_numpy(g).cuda())
+        hs.step = ref.step = step
+        kernels.multi_step(None, kernels.segment_array([ctypes.pointer(device_segment(hs, dev, pg))]))
+        assert oracle.multi_step([ref.ctype(og)], O.SIMD_AVX512) == 0
+    torch.cuda.synchronize()
+    assert from_device(hs, dev).mismatches(ref) == {}
+
+
 def test_pipeline_status_clear_after_all_updates(kernels):
     """No bounded pipeline wait gave up in any update of this session (the status word is still zero)."""
     assert kernels.pipeline_status() == 0
