@@ -251,6 +251,16 @@ __device__ __forceinline__ float scale_of(float amax)
     return __fmaf_rn(__fmaf_rn(-q0, fmax, amax), y, q0);
 }
 
+// Out-of-line copy of enc4_fp8 for the rare groups holding a NaN (kept out of the hot path's code).
+template <bool E4M3, bool SR>
+__device__ __noinline__ uint32_t enc4_fp8_slow(float x0, float x1, float x2, float x3, uint32_t r0, uint32_t r1,
+                                               uint32_t r2, uint32_t r3)
+{
+    const float x[4] = {x0, x1, x2, x3};     // scalar arguments: passed in registers, no local copies
+    const uint32_t r[4] = {r0, r1, r2, r3};
+    return enc4_fp8<E4M3, SR>(x, r);
+}
+
 // 4 floats -> 4 codes with the sign handled by the converter: the stochastic truncation only touches
 // significand bits (a carry out of them ends at the exponent, never in the sign bit, for any non-NaN
 // value), and cvt.rn.satfinite is symmetric in the sign, so sign | code(|t|) == cvt(t).  A NaN
@@ -276,7 +286,8 @@ __device__ __forceinline__ uint32_t enc4_signed(const float (&x)[4], const uint3
         asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(a[3]), "f"(a[2]));
     }
     const uint32_t w = (uint32_t)c01 | ((uint32_t)c23 << 16);
-    return nan ? enc4_fp8<E4M3, SR>(x, r) : w;
+    if (__builtin_expect(nan, 0)) return enc4_fp8_slow<E4M3, SR>(x[0], x[1], x[2], x[3], r[0], r[1], r[2], r[3]);
+    return w;
 }
 
 // ---- division by a block scale -------------------------------------------------------
@@ -288,6 +299,12 @@ __device__ __forceinline__ uint32_t enc4_signed(const float (&x)[4], const uint3
 // zero code whatever its last bits.  `fast_scale` tells whether s is in that range; otherwise the
 // caller divides with __fdiv_rn.
 __device__ __forceinline__ bool fast_scale(float s) { return s >= 0x1p-80f && s <= 0x1p100f; }
+
+// IEEE quotients for blocks whose scale is outside the fast range (out of line: rare).
+__device__ __noinline__ float4 div4_ieee(float4 x, float s)
+{
+    return make_float4(__fdiv_rn(x.x, s), __fdiv_rn(x.y, s), __fdiv_rn(x.z, s), __fdiv_rn(x.w, s));
+}
 
 __device__ __forceinline__ float div_by_scale(float x, float s, float y)
 {

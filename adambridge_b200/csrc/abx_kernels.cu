@@ -118,6 +118,14 @@ struct TileMeta {
     int64_t base;
 };
 
+// What consumers read per stage from shared memory: the tile's metadata and a copy of its segment's
+// descriptor (so the per-tile field reads are shared-memory broadcasts, not dependent parameter loads).
+struct __align__(16) StageHdr {
+    TileMeta meta;
+    KSeg seg;
+};
+constexpr int kHdrBytes = (int)sizeof(StageHdr);
+
 // ---- PTX: mbarriers and 1-D TMA bulk copies -----------------------------------------
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -411,13 +419,13 @@ template <bool E4M3, bool SR>
 __device__ __forceinline__ uint32_t encode4(const float (&x)[4], float s, int cnt, uint32_t idx0, uint32_t seed)
 {
     float q[4];
-    if (fast_scale(s)) {
+    if (__builtin_expect(fast_scale(s), 1)) {
         const float y = __frcp_rn(s);
 #pragma unroll
         for (int k = 0; k < 4; ++k) q[k] = div_by_scale(x[k], s, y);
     } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) q[k] = __fdiv_rn(x[k], s);
+        const float4 d = div4_ieee(make_float4(x[0], x[1], x[2], x[3]), s);
+        q[0] = d.x; q[1] = d.y; q[2] = d.z; q[3] = d.w;
     }
     uint32_t r[4];
 #pragma unroll
@@ -521,6 +529,12 @@ __device__ __forceinline__ int find_segment(const KArgs<NSEG>& a, int64_t t)
         if (a.seg[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
     }
     return lo;
+}
+
+// Dynamic shared memory: S full + S empty barriers, S stage headers, then the 128-byte-aligned ring.
+__host__ __device__ constexpr int ring_offset(int stages)
+{
+    return 128 * ((16 * ((16 * stages + 15) / 16) + stages * kHdrBytes + 127) / 128);
 }
 
 // A tile streams through shared memory when it is whole and every streamed buffer is 16-byte aligned.
@@ -636,13 +650,13 @@ template <bool E4M3, bool SR>
 __device__ __forceinline__ uint32_t fast_encode4(const float (&x)[4], float s, uint32_t idx0, uint32_t seed)
 {
     float q[4];
-    if (fast_scale(s)) {
+    if (__builtin_expect(fast_scale(s), 1)) {
         const float y = __frcp_rn(s);
 #pragma unroll
         for (int k = 0; k < 4; ++k) q[k] = div_by_scale(x[k], s, y);
     } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) q[k] = __fdiv_rn(x[k], s);
+        const float4 d = div4_ieee(make_float4(x[0], x[1], x[2], x[3]), s);
+        q[0] = d.x; q[1] = d.y; q[2] = d.z; q[3] = d.w;
     }
     uint32_t r[4];
 #pragma unroll
@@ -659,7 +673,7 @@ __device__ __forceinline__ void fast_fp8(const KSeg& S, int64_t base, const uint
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t blk0 = base >> 7;   // first block of the tile
     const float* swm = reinterpret_cast<const float*>(st + C::OFF_SM + (reinterpret_cast<uintptr_t>(S.m_scale + blk0) & 15));
-#pragma unroll
+#pragma unroll 1
     for (int h = 0; h < 2; ++h) {
         const int e0 = h * kHalf + threadIdx.x * kGroup;
         const int64_t i0 = base + e0;
@@ -744,8 +758,8 @@ __global__ void __launch_bounds__(kThreads, 3) update_kernel(const __grid_consta
     const int S = a.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + S;
-    TileMeta* meta = reinterpret_cast<TileMeta*>(empty + S);
-    uint8_t* ring = smem + 128 * ((32 * S + 127) / 128);
+    StageHdr* hdr = reinterpret_cast<StageHdr*>(smem + 16 * ((16 * S + 15) / 16));
+    uint8_t* ring = smem + ring_offset(S);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -768,9 +782,10 @@ __global__ void __launch_bounds__(kThreads, 3) update_kernel(const __grid_consta
             const KSeg& Sg = a.seg[si];
             const int64_t base = (t - Sg.tile_begin) * kTile;
             const bool staged = staged_tile(Sg, base);
-            meta[s].seg = si;
-            meta[s].staged = staged;
-            meta[s].base = base;
+            if (k < S || hdr[s].meta.seg != si) hdr[s].seg = Sg;   // the slot may hold this segment already
+            hdr[s].meta.seg = si;
+            hdr[s].meta.staged = staged;
+            hdr[s].meta.base = base;
             if (staged) {
                 uint8_t* st = ring + s * C::STAGE;
                 uint32_t bytes = C::ARR;
@@ -806,8 +821,8 @@ __global__ void __launch_bounds__(kThreads, 3) update_kernel(const __grid_consta
     for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
         const int s = k % S;
         if (!mbar_wait(&full[s], (k / S) & 1)) return;
-        const TileMeta tm = meta[s];
-        const KSeg& Sg = a.seg[tm.seg];
+        const TileMeta tm = hdr[s].meta;
+        const KSeg& Sg = hdr[s].seg;
         if (tm.staged) {
             const uint8_t* st = ring + s * C::STAGE;
             if (Sg.sr) fast_tile<ALGO, MV, PT, GT, true>(Sg, tm.base, st, gs);
@@ -889,7 +904,7 @@ int stages_of(int kind)
 size_t smem_of(int kind)
 {
     const int s = stages_of(kind);
-    return (size_t)(128 * ((32 * s + 127) / 128) + s * kStageBytes[kind]);
+    return (size_t)(ring_offset(s) + s * kStageBytes[kind]);
 }
 
 // Per-device launch geometry: SM count and resident CTAs per SM of each kernel.

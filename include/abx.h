@@ -175,6 +175,34 @@ int abx_multi_apply_scaled(void* stream, abx_segment* const* segs, const abx_hpa
 int abx_fused_adamw(float* p, const void* g, int g_dtype, void* m, void* v, int mv_dtype, void* out,
                     int out_dtype, int64_t n, uint64_t offset, const abx_hparams* hp, void* stream);
 
+/* ---- gradient norms and the clipping coefficient (not in the reference: its callers run
+ *      torch.nn.utils.clip_grad_norm_, which reads the gradients once for the norm and then reads
+ *      and writes them again to scale them) ----
+ * abx_clip_coef computes on the device, without a host synchronization:
+ *   sq[i]    = sum of squares of gradient i (fp32, fixed order: deterministic),
+ *   norms[i] = sqrt(sq[i]) rounded to the gradients' dtype (may be NULL),
+ *   total_coef[0] = the L2 norm of the norms, total_coef[1] = min(max_norm / (total + 1e-6), 1),
+ * each rounded as clip_grad_norm_ rounds it for that dtype (all gradients share one dtype).
+ * total_coef + 1 can be passed as abx_multi_step_scaled's g_scale: the update then applies the
+ * clipping while it reads the gradient.  `workspace` is device scratch of at least
+ * abx_clip_workspace_bytes(grads, n) bytes (16-byte aligned); too small: ABX_E_OOM.
+ * abx_grad_sq_norms / abx_clip_coef_from_sq are the two halves, for callers that sum the squared
+ * norms of sharded gradients across ranks in between. */
+typedef struct abx_tensor {
+    const void* data;    /* device pointer */
+    int64_t n;
+    int32_t dtype;       /* ABX_DT_F32 or ABX_DT_BF16 */
+    int32_t reserved;
+} abx_tensor;
+
+size_t abx_clip_workspace_bytes(const abx_tensor* grads, int32_t n);
+int abx_grad_sq_norms(void* stream, const abx_tensor* grads, int32_t n, float* sq, void* workspace,
+                      size_t workspace_bytes);
+int abx_clip_coef_from_sq(void* stream, const float* sq, int32_t n, int32_t dtype, float max_norm, float* norms,
+                          float* total_coef);
+int abx_clip_coef(void* stream, const abx_tensor* grads, int32_t n, float max_norm, float* sq, float* norms,
+                  float* total_coef, void* workspace, size_t workspace_bytes);
+
 /* Kernel launches this library has made in this process, all threads and devices. */
 uint64_t abx_launch_count(void);
 
