@@ -53,6 +53,7 @@ constexpr int kTile = 2 * kHalf;                       // 2048 elements per tile
 constexpr int kMaxSegs = 64;                           // segments per launch (parameter block ~10 KB)
 constexpr int kSmemTarget = 72 * 1024;                 // ring bytes per CTA (about three CTAs per SM)
 constexpr uint32_t kSpinLimit = 1u << 22;              // mbarrier polls before a wait gives up
+constexpr int kMaxReplicas = 7;                        // out replicas per segment (peers of an 8-GPU node)
 
 // Set (OR) by a CTA whose pipeline wait gave up; never set in correct operation.
 __device__ unsigned int g_pipeline_status;
@@ -77,6 +78,9 @@ struct KSeg {
     int32_t sr;
     int32_t vec_ok;           // 4-element vector access is aligned in every buffer (direct path)
     int32_t tma_ok;           // every streamed buffer is 16-byte aligned (bulk-copy path)
+    int32_t nrep;             // replicas of out: each out element is also stored at out + rep_delta[j] bytes
+    int32_t pad;
+    int64_t rep_delta[kMaxReplicas];
 };
 
 template <int NSEG>
@@ -316,12 +320,21 @@ __device__ __forceinline__ void store_master4(const KSeg& S, int64_t i0, int cnt
     }
 }
 
+// The new weights, into out and into each replica of out (peers' copies of the weights, written over
+// NVLink with plain stores: the fused all-gather of a sharded update).
 __device__ __forceinline__ void store_out4(const KSeg& S, int64_t i0, int cnt, const float (&p)[4])
 {
     if (S.out_dt == ABX_DT_BF16) {
-        st4_b16(static_cast<uint16_t*>(S.out) + i0, cnt, S.vec_ok, pack_bf16_rne(p[0], p[1]), pack_bf16_rne(p[2], p[3]));
+        const uint32_t w0 = pack_bf16_rne(p[0], p[1]), w1 = pack_bf16_rne(p[2], p[3]);
+        uint16_t* o = static_cast<uint16_t*>(S.out) + i0;
+        st4_b16(o, cnt, S.vec_ok, w0, w1);
+        for (int j = 0; j < S.nrep; ++j)
+            st4_b16(reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(o) + S.rep_delta[j]), cnt, S.vec_ok, w0, w1);
     } else if (S.out_dt == ABX_DT_F32) {
-        st4_f32(static_cast<float*>(S.out) + i0, cnt, S.vec_ok, p);
+        float* o = static_cast<float*>(S.out) + i0;
+        st4_f32(o, cnt, S.vec_ok, p);
+        for (int j = 0; j < S.nrep; ++j)
+            st4_f32(reinterpret_cast<float*>(reinterpret_cast<char*>(o) + S.rep_delta[j]), cnt, S.vec_ok, p);
     }
 }
 
@@ -834,6 +847,9 @@ __global__ void __launch_bounds__(kThreads, 3) update_kernel(const __grid_consta
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    // Stores into peers' memory (replicated out) are performed system-wide before this CTA ends, so the
+    // kernel's completion -- and any barrier the caller takes after it -- covers them.
+    __threadfence_system();
 }
 
 // ---- host side ---------------------------------------------------------------------------
@@ -998,8 +1014,10 @@ uint32_t hash32_host(uint32_t x)
 }
 
 void fill_kseg(KSeg& k, const abx_segment* s, const abx_hparams* h, int lanes, bool vec_ok, bool tma_ok,
-               int64_t tile_begin)
+               int64_t tile_begin, const int64_t* rep, int32_t nrep)
 {
+    k.nrep = s->out_dtype != ABX_DT_NONE ? nrep : 0;
+    for (int j = 0; j < k.nrep; ++j) k.rep_delta[j] = rep[j];
     const bool lion = s->algorithm == ABX_ALGO_LION;
     k.g = s->g;
     k.p = s->p;
@@ -1041,9 +1059,15 @@ int grid_for(int64_t tiles, int blocks_per_sm, int sms, int32_t max_ctas)
 
 // Validate everything, then launch kind by kind in batches of up to kMaxSegs.
 int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t nsegs, int32_t max_ctas,
-        const float* g_scale)
+        const float* g_scale, const int64_t* rep = nullptr, int32_t nrep = 0)
 {
     if (nsegs <= 0) return ABX_OK;
+    if (nrep < 0 || nrep > kMaxReplicas || (nrep > 0 && !rep)) return ABX_E_ARG;
+    for (int32_t j = 0; j < nrep; ++j)
+        if (rep[j] % 16) {
+            snprintf(g_err, sizeof g_err, "replica delta %lld is not a multiple of 16 bytes", (long long)rep[j]);
+            return ABX_E_ALIGN;
+        }
     if (!segs) return ABX_E_ARG;
     const bool from_groups = hps == nullptr;
     std::vector<char> vec_ok(nsegs), tma_ok(nsegs);
@@ -1086,7 +1110,7 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
                 KArgs<1> a;
                 std::memset(&a, 0, sizeof a);
                 const int32_t i = order[b];
-                fill_kseg(a.seg[0], segs[i], &hps[i], lanes, vec_ok[i], tma_ok[i], 0);
+                fill_kseg(a.seg[0], segs[i], &hps[i], lanes, vec_ok[i], tma_ok[i], 0, rep, nrep);
                 a.nseg = 1;
                 a.stages = stages_of(kind);
                 a.total_tiles = tiles_of(segs[i]->n);
@@ -1098,7 +1122,7 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
                 int64_t tiles = 0;
                 for (int j = 0; j < cnt; ++j) {
                     const int32_t i = order[b + j];
-                    fill_kseg(a.seg[j], segs[i], &hps[i], lanes, vec_ok[i], tma_ok[i], tiles);
+                    fill_kseg(a.seg[j], segs[i], &hps[i], lanes, vec_ok[i], tma_ok[i], tiles, rep, nrep);
                     tiles += tiles_of(segs[i]->n);
                 }
                 a.nseg = cnt;
@@ -1193,6 +1217,12 @@ ABX_API int abx_multi_step_scaled(void* stream, abx_segment* const* segs, int32_
                                   const float* g_scale)
 {
     return abx::run(stream, segs, nullptr, nsegs, max_ctas, g_scale);
+}
+
+ABX_API int abx_multi_step_replicated(void* stream, abx_segment* const* segs, int32_t nsegs, int32_t max_ctas,
+                                      const float* g_scale, const int64_t* out_deltas, int32_t nreplicas)
+{
+    return abx::run(stream, segs, nullptr, nsegs, max_ctas, g_scale, out_deltas, nreplicas);
 }
 
 ABX_API int abx_multi_apply_scaled(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t nsegs,

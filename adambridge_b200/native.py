@@ -192,6 +192,9 @@ class NativeKernels:
                                         ctypes.c_int32]
         lib.abx_multi_step_scaled.restype = ctypes.c_int
         lib.abx_multi_step_scaled.argtypes = [ctypes.c_void_p, seg_array, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
+        lib.abx_multi_step_replicated.restype = ctypes.c_int
+        lib.abx_multi_step_replicated.argtypes = [ctypes.c_void_p, seg_array, ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32]
         lib.abx_multi_apply_scaled.restype = ctypes.c_int
         lib.abx_multi_apply_scaled.argtypes = [ctypes.c_void_p, seg_array, ctypes.POINTER(_HParams), ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_void_p]
@@ -255,6 +258,16 @@ class NativeKernels:
             rc = self._lib.abx_multi_step_scaled(_stream_handle(stream), segments, len(segments), max_ctas,
                                                  _scale_ptr(g_scale))
         self._check(rc, "abx_multi_step")
+
+    def multi_step_replicated(self, stream, segments: ctypes.Array, out_deltas: list[int], max_ctas: int = 0,
+                              g_scale: torch.Tensor | None = None) -> None:
+        """multi_step, also storing every new weight at out + delta for each of ``out_deltas`` (bytes): the
+        peers' copies of a symmetric weight buffer (the all-gather of a sharded update, fused into it)."""
+        deltas = (ctypes.c_int64 * max(1, len(out_deltas)))(*out_deltas)
+        rc = self._lib.abx_multi_step_replicated(_stream_handle(stream), segments, len(segments), max_ctas,
+                                                 None if g_scale is None else _scale_ptr(g_scale), deltas,
+                                                 len(out_deltas))
+        self._check(rc, "abx_multi_step_replicated")
 
     def multi_apply(self, stream, segments: ctypes.Array, hparams: list, max_ctas: int = 0,
                     g_scale: torch.Tensor | None = None) -> None:

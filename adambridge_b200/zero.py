@@ -117,7 +117,11 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     ``step()``: the gradients in ``p.grad`` (every rank's full local gradients, as after backward) are averaged
     and scattered to their owners (NCCL reduce-scatter), each rank updates its shard, and the new weights are
-    all-gathered.  ``step_shard(grad_shard)``: the caller supplies this rank's already reduced gradient shard
+    all-gathered.  ``gather='p2p'`` (the default where the GPUs can map each other's memory) fuses the
+    all-gather into the update: the weight buffer lives in symmetric memory and the kernel stores each new
+    weight into every peer's copy over NVLink; ``'nccl'`` runs NCCL's all-gather round by round instead.
+
+    ``step_shard(grad_shard)``: the caller supplies this rank's already reduced gradient shard
     (``shard_numel`` elements, round-major; see :class:`FlatLayout`).  Every parameter is updated every step.
     """
 
@@ -126,7 +130,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     def __init__(self, params, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 1e-2, *, precision: str = "fp32", master_precision: str = "fp32",
                  stochastic_rounding: bool = True, seed: int = 0, process_group=None, rounds: int | None = None,
-                 max_ctas: int = 0, grad_dtype: torch.dtype | None = None):
+                 max_ctas: int = 0, grad_dtype: torch.dtype | None = None, gather: str = "auto"):
         if not 0.0 <= lr or not 0.0 <= eps or not 0.0 <= weight_decay:
             raise ValueError("lr, eps and weight_decay must be >= 0")
         if not 0.0 <= betas[0] < 1.0 or not 0.0 <= betas[1] < 1.0:
@@ -154,10 +158,25 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             raise TypeError(f"parameters must be bfloat16 or float32, got {dtype}")
         self.device, self.dtype = dev, dtype
         self.grad_dtype = grad_dtype or dtype
-        self.layout = FlatLayout([p.numel() for p in self._params], self.world, rounds)
+        if gather not in ("auto", "p2p", "nccl"):
+            raise ValueError("gather must be 'auto', 'p2p' or 'nccl'")
+        self._peer_deltas: list[int] | None = None
+        numels = [p.numel() for p in self._params]
+        flat = None
+        if self.world > 1 and gather != "nccl":
+            # fused all-gather: nothing to overlap round by round, so one round unless asked otherwise
+            self.layout = FlatLayout(numels, self.world, rounds or 1)
+            flat = self._symmetric_buffer(self.layout.total, dtype, dev, required=gather == "p2p")
+        if flat is None:
+            self.layout = FlatLayout(numels, self.world, rounds)
         L = self.layout
         with torch.no_grad(), torch.cuda.device(dev):
-            self.flat_weights = torch.zeros(L.total, dtype=dtype, device=dev)
+            if flat is None:
+                self.flat_weights = torch.zeros(L.total, dtype=dtype, device=dev)
+            else:
+                self.flat_weights = flat
+                self.flat_weights.zero_()
+                self._map_peers(flat)
             for i, p in enumerate(self._params):
                 a, b = L.flat_slice(i)
                 self.flat_weights[a:b].copy_(p.detach().view(-1))
@@ -176,6 +195,34 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._groups = [native.Group() for _ in self.param_groups]
         self._segs = self._build_segments()
         self.trace: list | None = None   # (start, end) CUDA events of every update launch, when a list
+
+    # ------------------------------------------------------------------ fused all-gather
+
+    @staticmethod
+    def _symmetric_buffer(numel: int, dtype, dev, required: bool):
+        """A buffer in symmetric memory (mapped into every peer), or None where the GPUs cannot map each
+        other's memory (then NCCL does the all-gather)."""
+        try:
+            import torch.distributed._symmetric_memory as symm
+            return symm.empty(numel, dtype=dtype, device=dev)
+        except Exception as exc:  # noqa: BLE001
+            if required:
+                raise RuntimeError(f"gather='p2p' needs symmetric memory: {exc}") from exc
+            return None
+
+    def _map_peers(self, flat: torch.Tensor) -> None:
+        import torch.distributed._symmetric_memory as symm
+        self._symm = symm.rendezvous(flat, group=self.pg)
+        ptrs = [int(x) for x in self._symm.buffer_ptrs]
+        base = ptrs[self.rank]
+        self._peer_deltas = [ptrs[r] - base for r in range(self.world) if r != self.rank]
+        self._barrier_flag = torch.zeros(1, dtype=torch.float32, device=flat.device)
+
+    def _barrier(self, stream) -> None:
+        """All ranks reach this point of their update streams (a one-element NCCL all-reduce: bounded by
+        the process group's timeout, no device-side spin)."""
+        with torch.cuda.stream(stream):
+            dist.all_reduce(self._barrier_flag, group=self.pg)
 
     # ------------------------------------------------------------------ segments
 
@@ -267,10 +314,13 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._refresh()
         cur = torch.cuda.current_stream(self.device)
         upd, comm = self._update_stream, self._comm_stream
+        p2p = self._peer_deltas is not None
         upd.wait_stream(cur)
         if comm is not None:
             comm.wait_stream(cur)
         with torch.cuda.device(self.device):
+            if p2p and flat_grads is None:
+                self._barrier(upd)   # no peer still reads the weights this update overwrites
             for r in range(L.rounds):
                 if flat_grads is not None:
                     shard = self.grad_shard[r * L.chunk:(r + 1) * L.chunk]
@@ -286,16 +336,21 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     start.record(upd)
                 if len(self._segs[r]):
-                    self.kernels.multi_step(upd, self._segs[r], self.max_ctas)
+                    if p2p:
+                        self.kernels.multi_step_replicated(upd, self._segs[r], self._peer_deltas, self.max_ctas)
+                    else:
+                        self.kernels.multi_step(upd, self._segs[r], self.max_ctas)
                 if end is not None:
                     end.record(upd)
                     self.trace.append((start, end))
-                if comm is not None:
+                if comm is not None and not p2p:
                     comm.wait_stream(upd)
                     with torch.cuda.stream(comm):
                         out = self.flat_weights[slice(*L.round_range(r))]
                         mine = self.flat_weights[slice(*L.rank_range(r, self.rank))]
                         dist.all_gather_into_tensor(out, mine, group=self.pg)
+        if p2p:
+            self._barrier(upd)       # every peer's stores into this rank's weights have landed
         cur.wait_stream(upd)
         if comm is not None:
             cur.wait_stream(comm)

@@ -213,7 +213,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     cls = ZeroLionBridge if algo == "lion" else ZeroAdamBridge
     kw = dict(lr=1e-5, betas=(0.9, 0.99), weight_decay=0.1) if algo == "lion" else \
         dict(lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
-    opt = cls(params, precision=prec, rounds=args.rounds, **kw)
+    opt = cls(params, precision=prec, rounds=args.rounds, max_ctas=args.max_ctas, gather=args.gather, **kw)
     L = opt.layout
     shard_params = sum(pc.n for r in opt._pieces for pc in r)
     with torch.no_grad():
@@ -307,7 +307,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         "config": {"workload": f"llama7b-{algo}-{prec}-moments" if dims == LLAMA7B else
                    f"llama-{dims['layers']}L-v{dims['vocab']}-{algo}-{prec}-moments", "params": n_params, "tensors": len(shapes),
                    "weights": "bf16", "grads": "bf16", "master": "fp32", "stochastic_rounding": True,
-                   "parallelism": f"zero1-dp{world}", "rounds": L.rounds,
+                   "parallelism": f"zero1-dp{world}", "rounds": L.rounds, "max_ctas": args.max_ctas,
+                   "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None,
                    "l2": "no flush: each step streams %.1f GB >> 126 MB L2" % (bpp * shard_params / 1e9)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None,
@@ -337,6 +338,9 @@ def main() -> int:
     ap.add_argument("--algorithm", default="adamw", choices=["adamw", "lion"])
     ap.add_argument("--precision", default="bf16", choices=["fp32", "bf16", "fp8"])
     ap.add_argument("--rounds", type=int, default=None)
+    ap.add_argument("--max-ctas", type=int, default=0, help="cap the update kernel's CTAs (0: every SM)")
+    ap.add_argument("--gather", default="auto", choices=["auto", "p2p", "nccl"],
+                    help="N > 1: all-gather fused into the update as peer stores (p2p), or NCCL's")
     ap.add_argument("--layers", type=int, default=None, help="override the decoder depth (small profiling cases)")
     ap.add_argument("--vocab", type=int, default=None, help="override the vocabulary (small profiling cases)")
     ap.add_argument("--e2e-steps", type=int, default=3)

@@ -169,6 +169,16 @@ int abx_multi_step_scaled(void* stream, abx_segment* const* segs, int32_t nsegs,
 int abx_multi_apply_scaled(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t nsegs,
                            int32_t max_ctas, const float* g_scale);
 
+/* abx_multi_step_replicated: abx_multi_step_scaled, and every `out` element is also stored at
+ * out + out_deltas[j] bytes for j < nreplicas (at most 7; each a multiple of 16).  With a weight
+ * buffer mapped at the same offsets on every GPU of a node (peer / symmetric memory), the deltas
+ * are the distances from this GPU's buffer to the peers': the sharded update then writes its new
+ * weights into every peer's copy over NVLink -- an all-gather fused into the update, with plain
+ * stores.  The caller orders the peers' later reads after the update (a barrier across ranks).
+ * Not in the reference (no multi-GPU code). */
+int abx_multi_step_replicated(void* stream, abx_segment* const* segs, int32_t nsegs, int32_t max_ctas,
+                              const float* g_scale, const int64_t* out_deltas, int32_t nreplicas);
+
 /* Single-tensor AdamW with fp32/bf16 moments and an fp32 master (replaces
  * adambridge_fused_adamw, adambridge_kernels.c:1518, same argument meaning and
  * error codes, plus the stream). */

@@ -69,7 +69,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, algo, precision, steps, out_dir):
+def _rank(rank, world, port, algo, precision, steps, out_dir, gather):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
@@ -77,7 +77,8 @@ def _rank(rank, world, port, algo, precision, steps, out_dir):
     try:
         params = _params(f"cuda:{rank}")
         cls = ZeroLionBridge if algo == "lion" else ZeroAdamBridge
-        opt = cls(params, lr=1e-3, precision=precision, seed=3, rounds=2)
+        opt = cls(params, lr=1e-3, precision=precision, seed=3, rounds=2, gather=gather)
+        assert (opt._peer_deltas is not None) == (gather == "p2p")
         for step in range(1, steps + 1):
             for p, g in zip(params, _grads(step, f"cuda:{rank}")):
                 p.grad = g
@@ -91,11 +92,14 @@ def _rank(rank, world, port, algo, precision, steps, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("algo,precision", [("adamw", "bf16"), ("adamw", "fp8")])
-def test_zero_two_gpus_nccl_equals_unsharded(tmp_path, algo, precision):
+@pytest.mark.parametrize("gather", ["nccl", "p2p"])
+@pytest.mark.parametrize("algo,precision", [("adamw", "bf16"), ("adamw", "fp8"), ("lion", "bf16")])
+def test_zero_two_gpus_equals_unsharded(tmp_path, algo, precision, gather):
+    """Reduce-scatter, sharded update and all-gather (NCCL's, or fused into the update as peer stores):
+    every rank ends with the unsharded update's weights, bit for bit."""
     steps = 3
     want_w, _ = _reference(algo, precision, steps, "cuda:0")
-    mp.start_processes(_rank, args=(2, _free_port(), algo, precision, steps, str(tmp_path)), nprocs=2,
+    mp.start_processes(_rank, args=(2, _free_port(), algo, precision, steps, str(tmp_path), gather), nprocs=2,
                        start_method="spawn", join=True)
     for r in range(2):
         got = pickle.load(open(tmp_path / f"rank{r}.pkl", "rb"))
