@@ -20,7 +20,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -55,54 +54,50 @@ def numel(shape):
 # --------------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    """SM clock and clock-event (throttle) reasons of one GPU, sampled through NVML every 10 ms on a thread
+    while the timed region runs (read-only queries; nothing is set)."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+    def __init__(self, index: int, period: float = 0.01):
+        self.index, self.period = index, period
+        self.mhz, self.reasons, self.max_mhz = [], set(), None
+
+    def _loop(self):
+        import pynvml
+        h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        bits = {name: getattr(pynvml, attr) for name, attr in self.REASONS.items()}
+        while not self._stop.is_set():
+            self.mhz.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+            active = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.reasons.update(name for name, bit in bits.items() if active & bit)
+            self._stop.wait(self.period)
 
     def __enter__(self):
+        import threading
+        self._stop = threading.Event()
+        self._thread = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001 -- no NVML: the line reports no samples
+            self._thread = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
-        else:
-            self.lines = []
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        mhz, mx, reasons = [], None, set()
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                mhz.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[3:7]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(mhz)}
+        return {"sm_mhz": statistics.median(self.mhz) if self.mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.mhz)}
 
 
 # --------------------------------------------------------------------------- CPU baseline
@@ -223,6 +218,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
 
     def step():
+        if args.clip is not None:
+            opt.clip_shard_grad_norm_(args.clip)
         opt.step_shard()
 
     for _ in range(args.warmup):
@@ -247,12 +244,13 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     launches = kern.launch_count() - launches0
     ms = t0.elapsed_time(t1) / args.steps
     kernel_ms = sum(s.elapsed_time(e) for s, e in opt.trace) / args.steps
+    norm_ms = sum(s.elapsed_time(e) for s, e in opt.norm_trace) / args.steps
     n_launches_trace = len(opt.trace)
     opt.trace = None
-    ms_t = torch.tensor([ms, kernel_ms], dtype=torch.float64, device=dev)
+    ms_t = torch.tensor([ms, kernel_ms, norm_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max, kernel_ms_max = ms_t.tolist()
+    ms_max, kernel_ms_max, norm_ms_max = ms_t.tolist()
 
     # ---- e2e: host buffers through the public API (pinned grad shard in, updated weight shard out)
     e2e = None
@@ -265,6 +263,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
 
         def e2e_step():
             opt.grad_shard.copy_(host_g, non_blocking=True)
+            if args.clip is not None:
+                opt.clip_shard_grad_norm_(args.clip)
             opt.step_shard()
             for r, w in enumerate(mine):
                 host_w[r * L.chunk:(r + 1) * L.chunk].copy_(w, non_blocking=True)
@@ -304,8 +304,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         "value": round(n_params / (ms_max / 1e3) / 1e9, 4), "unit": "Gparams/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"llama7b-{algo}-{prec}-moments" if dims == LLAMA7B else
-                   f"llama-{dims['layers']}L-v{dims['vocab']}-{algo}-{prec}-moments", "params": n_params, "tensors": len(shapes),
+        "config": {"workload": (f"llama7b-{algo}-{prec}-moments" if dims == LLAMA7B else
+                                f"llama-{dims['layers']}L-v{dims['vocab']}-{algo}-{prec}-moments")
+                   + ("" if args.clip is None else f"-clip{args.clip:g}"), "params": n_params, "tensors": len(shapes),
                    "weights": "bf16", "grads": "bf16", "master": "fp32", "stochastic_rounding": True,
                    "parallelism": f"zero1-dp{world}", "rounds": L.rounds, "max_ctas": args.max_ctas,
                    "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None,
@@ -319,6 +320,12 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
+    if args.clip is not None:
+        g_bytes = shard_params * opt.grad_shard.element_size()
+        line["clip"] = {"max_norm": args.clip, "norm_kernels_ms": round(norm_ms_max, 3),
+                        "norm_gbs": round(g_bytes / (norm_ms_max / 1e3) / 1e9, 1),
+                        "basis": "clip_shard_grad_norm_ before every step: one read of the bf16 gradient shard "
+                                 "(per-tensor sums of squares), the coefficient applied inside the update kernel"}
     if world > 1:
         line["allgather"] = {"bytes_received_per_rank": int((world - 1) * L.chunk * L.rounds * 2),
                              "step_ms": round(ms_max, 3), "update_kernel_ms": round(kernel_ms_max, 3)}
@@ -343,6 +350,8 @@ def main() -> int:
                     help="N > 1: all-gather fused into the update as peer stores (p2p), or NCCL's")
     ap.add_argument("--layers", type=int, default=None, help="override the decoder depth (small profiling cases)")
     ap.add_argument("--vocab", type=int, default=None, help="override the vocabulary (small profiling cases)")
+    ap.add_argument("--clip", type=float, default=None,
+                    help="clip_grad_norm_ to this max norm before every step (norm kernels + scaled update)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -362,6 +371,8 @@ def main() -> int:
     import torch
     import torch.distributed as dist
     if world > 1:
+        # NCCL's own banner would precede the result line on stdout
+        os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
