@@ -55,6 +55,13 @@ class BuildError(RuntimeError):
     pass
 
 
+class Tensor(ctypes.Structure):
+    """One gradient for the norm kernels (abx_tensor): device pointer, elements, dtype code."""
+
+    _fields_ = [("data", ctypes.c_void_p), ("n", ctypes.c_int64), ("dtype", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
 class _HParams(ctypes.Structure):
     _fields_ = [
         ("beta1", ctypes.c_float),
@@ -209,6 +216,18 @@ class NativeKernels:
         lib.abx_last_error.restype = ctypes.c_char_p
         lib.abx_launch_count.restype = ctypes.c_uint64
         lib.abx_pipeline_status.restype = ctypes.c_int
+        tens = ctypes.POINTER(Tensor)
+        lib.abx_clip_workspace_bytes.restype = ctypes.c_size_t
+        lib.abx_clip_workspace_bytes.argtypes = [tens, ctypes.c_int32]
+        lib.abx_grad_sq_norms.restype = ctypes.c_int
+        lib.abx_grad_sq_norms.argtypes = [ctypes.c_void_p, tens, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_size_t]
+        lib.abx_clip_coef_from_sq.restype = ctypes.c_int
+        lib.abx_clip_coef_from_sq.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]
+        lib.abx_clip_coef.restype = ctypes.c_int
+        lib.abx_clip_coef.argtypes = [ctypes.c_void_p, tens, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
         self._lib = lib
 
     # -- rounding pattern ----------------------------------------------------
@@ -291,6 +310,33 @@ class NativeKernels:
     def launch_count(self) -> int:
         """Kernel launches made by libabx in this process so far."""
         return self._lib.abx_launch_count()
+
+    # -- gradient norms and the clipping coefficient ---------------------------
+
+    @staticmethod
+    def tensor_array(tensors: list[torch.Tensor]) -> ctypes.Array:
+        arr = (Tensor * max(1, len(tensors)))()
+        for i, t in enumerate(tensors):
+            if not t.is_cuda or not t.is_contiguous():
+                raise ValueError("gradients must be contiguous CUDA tensors")
+            arr[i] = Tensor(t.data_ptr(), t.numel(), dtype_code_of(t.dtype), 0)
+        return arr
+
+    def clip_workspace_bytes(self, arr: ctypes.Array, n: int) -> int:
+        return self._lib.abx_clip_workspace_bytes(arr, n)
+
+    def grad_sq_norms(self, stream, arr: ctypes.Array, n: int, sq: torch.Tensor, workspace: torch.Tensor) -> None:
+        """sq[i] = sum of squares of gradient i (fp32, deterministic order)."""
+        rc = self._lib.abx_grad_sq_norms(_stream_handle(stream), arr, n, sq.data_ptr(), workspace.data_ptr(),
+                                         workspace.numel() * workspace.element_size())
+        self._check(rc, "abx_grad_sq_norms")
+
+    def clip_coef_from_sq(self, stream, sq: torch.Tensor, dtype: torch.dtype, max_norm: float,
+                          norms: torch.Tensor | None, total_coef: torch.Tensor) -> None:
+        rc = self._lib.abx_clip_coef_from_sq(_stream_handle(stream), sq.data_ptr(), sq.numel(), dtype_code_of(dtype),
+                                             float(max_norm), None if norms is None else norms.data_ptr(),
+                                             total_coef.data_ptr())
+        self._check(rc, "abx_clip_coef_from_sq")
 
     def pipeline_status(self) -> int:
         """Nonzero if an update kernel's bounded pipeline wait gave up since the last call (then cleared).

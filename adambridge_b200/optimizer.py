@@ -10,6 +10,7 @@ from typing import Any, Callable, Iterable
 
 import torch
 
+from .clip import clip_coefficient
 from .engine import ParamSlot, SmallGroup, StepStats, UpdateEngine
 from .precision import (FP32Store, _checked, bytes_per_param, canonical_master_precision, canonical_precision,
                         check_master_state, load_master_, make_store, master_to_fp32, store_from_state_dict)
@@ -34,9 +35,10 @@ class AdamBridge(torch.optim.Optimizer):
         loss.backward(); opt.step_sync()                      # GPU as soon as its gradient is complete
 
     In hook mode gradients are released as soon as the update kernel has been enqueued
-    (``release_grads=True``).  Global gradient clipping needs every gradient first: use ``step()`` after
-    ``clip_grad_norm_``, or pass the clip factor as a device scalar (``step(grad_scale=...)``), which the kernel
-    applies while it reads the gradient.
+    (``release_grads=True``).  Global gradient clipping needs every gradient first: in ``step()`` mode call
+    ``opt.clip_grad_norm_(max_norm)`` (torch's ``clip_grad_norm_``, with the gradients scaled inside the next
+    update instead of in place), or ``torch.nn.utils.clip_grad_norm_`` as usual, or pass any factor as a
+    device scalar (``step(grad_scale=...)``).
 
     Args mirror the reference (adambridge/optimizer.py:126-151).  ``precision``: moment storage, ``'fp32'``,
     ``'bf16'`` (``'bf16_moments'``) or ``'fp8'`` (``'fp8_moments'``).  ``master_precision``: ``'fp32'`` or
@@ -117,6 +119,7 @@ class AdamBridge(torch.optim.Optimizer):
         self._steps_synced = 0
         self.last_step_stats: StepStats | None = None
         self._autotune_requested = bool(autotune)
+        self._clip_coef: torch.Tensor | None = None
 
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
 
@@ -276,10 +279,40 @@ class AdamBridge(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        if self._clip_coef is not None:
+            if grad_scale is not None:
+                raise ValueError("step(grad_scale=...) after clip_grad_norm_(): the clip coefficient is the scale")
+            grad_scale, self._clip_coef = self._clip_coef, None
         self._submit_remaining(grad_scale)
         self._flush_small(release=False, g_scale=grad_scale)
         self.step_sync()
         return loss
+
+    @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float, norm_type: float = 2.0, error_if_nonfinite: bool = False,
+                        foreach: bool | None = None) -> torch.Tensor:
+        """``torch.nn.utils.clip_grad_norm_`` over this optimizer's gradients, fused into the next :meth:`step`.
+
+        Returns the total L2 norm (a device tensor in the gradients' dtype, as torch returns it) without a host
+        synchronization.  The gradients are not modified: the next ``step()`` multiplies each one by the clipping
+        coefficient inside the update kernel, rounding to the gradient's dtype exactly as torch's in-place
+        multiply does, so ``opt.clip_grad_norm_(c); opt.step()`` equals ``clip_grad_norm_(params, c); opt.step()``.
+        The norms come from libabx's multi-tensor norm kernels (one read of the gradients).  Only the L2 norm is
+        fused; all gradients must share one dtype.  ``error_if_nonfinite`` synchronizes to check the norm."""
+        del foreach
+        if float(norm_type) != 2.0:
+            raise ValueError("AdamBridge.clip_grad_norm_ computes the L2 norm (norm_type=2) only")
+        if any(slot.submitted for slot in self._ordered):
+            raise RuntimeError("clip_grad_norm_ after a hook already updated parameters: clip before any update")
+        grads = [slot.param.grad for slot in self._ordered if slot.param.grad is not None]
+        if not grads:
+            return torch.tensor(0.0)
+        total, coef, _ = clip_coefficient(grads, max_norm, kernels=self._engine.native)
+        if error_if_nonfinite and not torch.isfinite(total).item():
+            raise RuntimeError(f"The total norm of order 2.0 for gradients from `parameters` is non-finite, "
+                               "so it cannot be clipped.")
+        self._clip_coef = coef
+        return total
 
     # ------------------------------------------------------------- precision
 

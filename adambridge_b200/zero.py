@@ -34,7 +34,8 @@ import torch
 import torch.distributed as dist
 
 from . import native
-from .precision import canonical_master_precision, canonical_precision, make_master, make_store
+from .precision import (FP8Store, FP24Store, FP32Store, _checked, canonical_master_precision, canonical_precision,
+                        check_master_state, load_master_, make_master, make_store, store_from_state_dict)
 
 __all__ = ["FlatLayout", "Piece", "ZeroAdamBridge", "ZeroLionBridge"]
 
@@ -106,6 +107,23 @@ class FlatLayout:
 
     def flat_slice(self, index: int) -> tuple[int, int]:
         return self.offsets[index], self.offsets[index] + self.numels[index]
+
+    def shard_runs(self, rank: int, unit: int = 1, padded: bool = False) -> list[tuple[int, int, int, int]]:
+        """``(index, param_lo, shard_lo, length)`` for every piece of ``rank``'s shard, in entries of an array
+        holding one entry per ``unit`` elements (1: weights, master, moments; 128: FP8 block scales).
+        ``padded`` extends each tensor's last piece to its last whole 128-element block (FP8 codes and scales,
+        which a per-tensor store keeps padded).  Pieces start on 128-element boundaries of their tensor, so
+        the runs are exact in either unit."""
+        if unit not in (1, ALIGN):
+            raise ValueError(f"unit must be 1 or {ALIGN}")
+        runs = []
+        for rnd in self.pieces(rank):
+            for pc in rnd:
+                hi = pc.t_hi
+                if (padded or unit > 1) and hi == self.numels[pc.index]:
+                    hi = -(-hi // ALIGN) * ALIGN
+                runs.append((pc.index, pc.t_lo // unit, pc.local_lo // unit, (hi - pc.t_lo) // unit))
+        return runs
 
 
 class ZeroAdamBridge(torch.optim.Optimizer):
@@ -195,6 +213,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._groups = [native.Group() for _ in self.param_groups]
         self._segs = self._build_segments()
         self.trace: list | None = None   # (start, end) CUDA events of every update launch, when a list
+        self.norm_trace: list = []       # (start, end) events of the norm kernels, while ``trace`` is a list
+        self._clip_coef: torch.Tensor | None = None
+        self._norm_state = None
 
     # ------------------------------------------------------------------ fused all-gather
 
@@ -284,13 +305,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             self._flat_grads = torch.zeros(self.layout.total, dtype=self.grad_dtype, device=self.device)
         return self._flat_grads
 
-    @torch.no_grad()
-    def step(self, closure=None):
-        """Reduce-scatter (mean) the local gradients, update this rank's shard, all-gather the weights."""
-        loss = None
-        if closure is not None:
-            with torch.enable_grad():
-                loss = closure()
+    def _local_grads(self) -> torch.Tensor:
+        """Every parameter's local gradient in the flat gradient buffer (no copy where p.grad views it)."""
         L = self.layout
         flat = self._flat_grad_buffer()
         for i, p in enumerate(self._params):
@@ -299,7 +315,21 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             a, b = L.flat_slice(i)
             if p.grad.data_ptr() != flat[a:b].data_ptr():
                 flat[a:b].copy_(p.grad.reshape(-1))
-        self._run(flat)
+        return flat
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        """Reduce-scatter (mean) the local gradients, update this rank's shard, all-gather the weights.
+        After :meth:`clip_grad_norm_` the gradients are already reduced and the update applies the clip."""
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        if self._clip_coef is not None:
+            coef, self._clip_coef = self._clip_coef, None
+            self._run(None, g_scale=coef, synced=True)
+        else:
+            self._run(self._local_grads())
         return loss
 
     @torch.no_grad()
@@ -307,9 +337,102 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         """Update from this rank's reduced gradient shard (default: ``self.grad_shard``) and all-gather."""
         if grad_shard is not None and grad_shard.data_ptr() != self.grad_shard.data_ptr():
             self.grad_shard.copy_(grad_shard)
-        self._run(None)
+        if self._clip_coef is not None:
+            coef, self._clip_coef = self._clip_coef, None
+            self._run(None, g_scale=coef, synced=True)
+        else:
+            self._run(None)
 
-    def _run(self, flat_grads: torch.Tensor | None) -> None:
+    # ------------------------------------------------------------------ clipping
+
+    def _norm_inputs(self):
+        """Built once: this rank's pieces as norm-kernel tensors over ``grad_shard``, the kernel workspace, the
+        per-piece sums (plus a zero slot) and, per parameter, the indices of its pieces here (padded with the
+        zero slot) -- so the per-parameter partial sums are a fixed-order gather and sum."""
+        if self._norm_state is None:
+            pieces = [pc for rnd in self._pieces for pc in rnd]
+            es = self.grad_shard.element_size()
+            code = native.dtype_code_of(self.grad_dtype)
+            arr = (native.Tensor * max(1, len(pieces)))()
+            for j, pc in enumerate(pieces):
+                arr[j] = native.Tensor(self.grad_shard.data_ptr() + pc.local_lo * es, pc.n, code, 0)
+            owned: list[list[int]] = [[] for _ in self._params]
+            for j, pc in enumerate(pieces):
+                owned[pc.index].append(j)
+            width = max(1, max(len(o) for o in owned))
+            idx = [o + [len(pieces)] * (width - len(o)) for o in owned]
+            dev = self.device
+            ws = torch.empty(self.kernels.clip_workspace_bytes(arr, len(pieces)), dtype=torch.uint8, device=dev)
+            sq_ext = torch.zeros(len(pieces) + 1, dtype=torch.float32, device=dev)
+            self._norm_state = (arr, len(pieces), ws, sq_ext, torch.tensor(idx, dtype=torch.long, device=dev))
+        return self._norm_state
+
+    @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float, norm_type: float = 2.0) -> torch.Tensor:
+        """``torch.nn.utils.clip_grad_norm_`` of the averaged gradient, fused into the next :meth:`step`.
+
+        Reduce-scatters (mean) the local gradients now, sums the squares of this rank's pieces of every
+        parameter (libabx norm kernels), all-reduces the per-parameter sums (one small NCCL all-reduce) and
+        computes the per-parameter norms, the total norm and the coefficient as torch does in the gradients'
+        dtype.  Returns the total norm as a device tensor; the next ``step()`` updates from the reduced shard
+        with every gradient scaled by the coefficient inside the update kernel."""
+        if float(norm_type) != 2.0:
+            raise ValueError("clip_grad_norm_ computes the L2 norm (norm_type=2) only")
+        flat = self._local_grads()
+        L = self.layout
+        cur = torch.cuda.current_stream(self.device)
+        upd, comm = self._update_stream, self._comm_stream
+        upd.wait_stream(cur)
+        with torch.cuda.device(self.device):
+            if comm is None:
+                with torch.cuda.stream(upd):
+                    for r in range(L.rounds):
+                        self.grad_shard[r * L.chunk:(r + 1) * L.chunk].copy_(flat[slice(*L.round_range(r))])
+            else:
+                comm.wait_stream(cur)
+                with torch.cuda.stream(comm):
+                    for r in range(L.rounds):
+                        dist.reduce_scatter_tensor(self.grad_shard[r * L.chunk:(r + 1) * L.chunk],
+                                                   flat[slice(*L.round_range(r))], op=dist.ReduceOp.AVG,
+                                                   group=self.pg)
+                upd.wait_stream(comm)
+        return self._clip_shard(max_norm, cur)
+
+    @torch.no_grad()
+    def clip_shard_grad_norm_(self, max_norm: float, grad_shard: torch.Tensor | None = None) -> torch.Tensor:
+        """:meth:`clip_grad_norm_` for the :meth:`step_shard` path: the norm of the reduced gradient whose shards
+        the ranks hold (``grad_shard``, default ``self.grad_shard``); the next ``step_shard()`` applies the clip."""
+        cur = torch.cuda.current_stream(self.device)
+        if grad_shard is not None and grad_shard.data_ptr() != self.grad_shard.data_ptr():
+            self.grad_shard.copy_(grad_shard)
+        self._update_stream.wait_stream(cur)
+        return self._clip_shard(max_norm, cur)
+
+    def _clip_shard(self, max_norm: float, cur) -> torch.Tensor:
+        """Norms of ``grad_shard`` on the update stream; keeps the coefficient for the next update."""
+        upd = self._update_stream
+        with torch.cuda.device(self.device):
+            arr, npieces, ws, sq_ext, idx = self._norm_inputs()
+            start = end = None
+            if self.trace is not None:
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record(upd)
+            self.kernels.grad_sq_norms(upd, arr, npieces, sq_ext, ws)
+            if end is not None:
+                end.record(upd)
+                self.norm_trace.append((start, end))
+            with torch.cuda.stream(upd):
+                sq = sq_ext[idx].sum(dim=1)
+                if self._comm_stream is not None:
+                    dist.all_reduce(sq, group=self.pg)   # also orders every rank's update after all backward passes
+                total_coef = torch.empty(2, dtype=torch.float32, device=self.device)
+            self.kernels.clip_coef_from_sq(upd, sq, self.grad_dtype, max_norm, None, total_coef)
+        cur.wait_stream(upd)
+        self._clip_coef = total_coef[1:2]
+        return total_coef[0].to(self.grad_dtype)
+
+    def _run(self, flat_grads: torch.Tensor | None, g_scale: torch.Tensor | None = None,
+             synced: bool = False) -> None:
         L = self.layout
         self._refresh()
         cur = torch.cuda.current_stream(self.device)
@@ -319,7 +442,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         if comm is not None:
             comm.wait_stream(cur)
         with torch.cuda.device(self.device):
-            if p2p and flat_grads is None:
+            if p2p and flat_grads is None and not synced:
                 self._barrier(upd)   # no peer still reads the weights this update overwrites
             for r in range(L.rounds):
                 if flat_grads is not None:
@@ -337,9 +460,10 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                     start.record(upd)
                 if len(self._segs[r]):
                     if p2p:
-                        self.kernels.multi_step_replicated(upd, self._segs[r], self._peer_deltas, self.max_ctas)
+                        self.kernels.multi_step_replicated(upd, self._segs[r], self._peer_deltas, self.max_ctas,
+                                                           g_scale)
                     else:
-                        self.kernels.multi_step(upd, self._segs[r], self.max_ctas)
+                        self.kernels.multi_step(upd, self._segs[r], self.max_ctas, g_scale)
                 if end is not None:
                     end.record(upd)
                     self.trace.append((start, end))
@@ -367,8 +491,158 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         rep["total"] = sum(rep.values())
         return rep
 
-    def state_dict(self) -> dict[str, Any]:
-        raise NotImplementedError("ZeroAdamBridge checkpoints: gather with AdamBridge-format shards is not built yet")
+    # ------------------------------------------------------------------ checkpoints
+
+    CKPT_ENTRIES = 1 << 25   # shard entries gathered per collective: bounds the temporary buffers
+
+    @staticmethod
+    def _planes(store) -> list[tuple[torch.Tensor, int, bool]]:
+        """A store's arrays as (tensor, unit, padded) in the sense of :meth:`FlatLayout.shard_runs`."""
+        if isinstance(store, FP8Store):
+            return [(store.q, 1, True), (store.scale, ALIGN, True)]
+        if isinstance(store, FP24Store):
+            return [(store.hi, 1, False), (store.lo, 1, False)]
+        return [(store.data, 1, False)]
+
+    @staticmethod
+    def _raw(t: torch.Tensor) -> torch.Tensor:
+        """Same bytes as an integer tensor (collectives and copies move bits, never convert values)."""
+        return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
+
+    def _gather_plane(self, shard: torch.Tensor, dests: list[torch.Tensor], unit: int, padded: bool,
+                      keep: bool) -> None:
+        """Every rank's ``shard`` array, gathered ``CKPT_ENTRIES`` entries at a time, copied into the
+        per-parameter host arrays ``dests`` (when ``keep``)."""
+        L = self.layout
+        runs = [L.shard_runs(k, unit, padded) for k in range(self.world)]
+        raw = self._raw(shard)
+        dst = [self._raw(d) for d in dests]
+        n = raw.numel()
+        for s0 in range(0, n, self.CKPT_ENTRIES):
+            s1 = min(n, s0 + self.CKPT_ENTRIES)
+            if self.world == 1:
+                out = raw[s0:s1].unsqueeze(0)
+            else:
+                out = torch.empty((self.world, s1 - s0), dtype=raw.dtype, device=self.device)
+                dist.all_gather_into_tensor(out, raw[s0:s1].contiguous(), group=self.pg)
+            if not keep:
+                continue
+            host = out.cpu()
+            for k in range(self.world):
+                for index, p_lo, s_lo, length in runs[k]:
+                    a, b = max(s_lo, s0), min(s_lo + length, s1)
+                    if a < b:
+                        dst[index][p_lo + a - s_lo:p_lo + b - s_lo].copy_(host[k, a - s0:b - s0])
+
+    @torch.no_grad()
+    def state_dict(self, rank0_only: bool = False) -> dict[str, Any]:
+        """The AdamBridge checkpoint format (adambridge/optimizer.py:525-544): per-parameter master weights and
+        moments, assembled from every rank's shard into host tensors -- loadable by ``AdamBridge`` and by a
+        ZeRO optimizer of any world size.  Collective: every rank of the group must call it.  With
+        ``rank0_only`` the other ranks take part in the gathers and return an empty ``state``."""
+        torch.cuda.current_stream(self.device).wait_stream(self._update_stream)
+        sd = super().state_dict()
+        sd["state"] = {}
+        keep = not rank0_only or self.rank == 0
+        L = self.layout
+        masters = [make_master(self.master_precision, n, device="cpu") for n in L.numels]
+        stores = [("exp_avg", self.m, [make_store(self.precision, n, "m", device="cpu") for n in L.numels])]
+        if self.v is not None:
+            stores.append(("exp_avg_sq", self.v, [make_store(self.precision, n, "v", device="cpu") for n in L.numels]))
+        for shard_store, per_param in [(self.master, masters)] + [(st, pp) for _, st, pp in stores]:
+            for j, (plane, unit, padded) in enumerate(self._planes(shard_store)):
+                self._gather_plane(plane, [self._planes(p)[j][0] for p in per_param], unit, padded, keep)
+        if keep and self.step_count > 0:
+            for i in range(len(self._params)):
+                m = masters[i]
+                st = sd["state"][i] = {"step": self.step_count,
+                                       "master": m.data if isinstance(m, FP32Store) else m.state_dict()}
+                for key, _, per_param in stores:
+                    st[key] = per_param[i].state_dict()
+        sd["adambridge"] = {"precision": self.precision, "master_precision": self.master_precision, "format": 1,
+                            "algorithm": self._algorithm}
+        return sd
+
+    @torch.no_grad()
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:
+        """Load an AdamBridge / ZeRO checkpoint (the reference's dict format, any world size) or a
+        ``torch.optim.AdamW`` one: every rank reads the whole checkpoint and keeps its own pieces; moments and
+        master are converted to this optimizer's precisions.  The weights are the model's to load."""
+        saved = {int(k) if isinstance(k, str) and k.isdigit() else k: v for k, v in state_dict["state"].items()}
+        L = self.layout
+        lion = self._algorithm == "lion"
+        for index, st in saved.items():
+            if isinstance(index, bool) or not isinstance(index, int) or not 0 <= index < len(self._params):
+                raise ValueError(f"checkpoint state for parameter {index!r}: this optimizer has parameters "
+                                 f"0..{len(self._params) - 1}")
+            numel = L.numels[index]
+            if st.get("master") is not None:
+                check_master_state(st["master"], numel, f"master weights of parameter {index}")
+            for key in ("exp_avg", "exp_avg_sq"):
+                if key in st:
+                    _check_moment_state(st[key], numel, f"{key} of parameter {index}")
+            if "exp_avg" not in st or (not lion and "exp_avg_sq" not in st):
+                raise ValueError("checkpoint has no exp_avg / exp_avg_sq (saved by LionBridge?); AdamW needs both")
+        if saved and len(saved) != len(self._params):
+            raise ValueError(f"checkpoint holds state for {len(saved)} of {len(self._params)} parameters; a ZeRO "
+                             "optimizer updates every parameter every step and needs all of them")
+        steps = {int(st["step"].item() if isinstance(st["step"], torch.Tensor) else st["step"]) for st in saved.values()}
+        if len(steps) > 1:
+            raise ValueError(f"checkpoint parameters are at different steps {sorted(steps)}; ZeRO needs one")
+        super().load_state_dict({"state": {}, "param_groups": state_dict["param_groups"]})
+        dev = self.device
+        runs = {}
+        for unit, padded in ((1, False), (1, True), (ALIGN, True)):
+            for index, p_lo, s_lo, length in L.shard_runs(self.rank, unit, padded):
+                runs.setdefault((unit, padded, index), []).append((p_lo, s_lo, length))
+
+        def scatter(shard_store, param_store, index):
+            for (plane, unit, padded), (src, _, _) in zip(self._planes(shard_store), self._planes(param_store)):
+                raw, rsrc = self._raw(plane), self._raw(src)
+                for p_lo, s_lo, length in runs.get((unit, padded, index), []):
+                    raw[s_lo:s_lo + length].copy_(rsrc[p_lo:p_lo + length])
+
+        with torch.cuda.device(dev):
+            for index, st in saved.items():
+                numel = L.numels[index]
+                if st.get("master") is not None:
+                    master = make_master(self.master_precision, numel, device=dev)
+                    load_master_(master, st["master"])
+                    scatter(self.master, master, index)
+                for key, shard_store, role in (("exp_avg", self.m, "m"), ("exp_avg_sq", self.v, "v")):
+                    if shard_store is None:
+                        continue
+                    scatter(shard_store, self._load_store(st[key], numel, role, dev), index)
+        if saved:
+            self.step_count = steps.pop()
+        torch.cuda.synchronize(dev)
+
+    def _load_store(self, saved, numel: int, role: str, device):
+        if isinstance(saved, torch.Tensor):  # torch.optim.AdamW layout
+            return make_store(self.precision, numel, role, init=saved.to(device, torch.float32), device=device)
+        store = store_from_state_dict(saved, numel, role, device=device)
+        if store.precision != self.precision:
+            store = make_store(self.precision, numel, role, init=store.to_fp32(), device=device)
+        return store
+
+
+def _check_moment_state(saved: Any, numel: int, what: str) -> None:
+    """Sizes of a checkpoint's moment store (a tensor, or an fp32/bf16/fp8 store dict), checked before anything
+    is loaded, so a mismatched checkpoint changes nothing."""
+    if isinstance(saved, torch.Tensor):
+        _checked(saved, numel, what)
+        return
+    if not isinstance(saved, dict) or saved.get("precision") not in ("fp32", "bf16", "fp8"):
+        raise ValueError(f"checkpoint {what}: unknown moment store")
+    if saved["precision"] != "fp8":
+        _checked(saved.get("data"), numel, what)
+        return
+    block = saved.get("block")
+    if not isinstance(block, int) or isinstance(block, bool) or not 0 < block <= 1 << 20:
+        raise ValueError(f"checkpoint {what}: invalid FP8 block size {block!r}")
+    nblocks = max(1, -(-numel // block))
+    _checked(saved.get("q"), nblocks * block, f"{what} (FP8 codes)")
+    _checked(saved.get("scale"), nblocks, f"{what} (FP8 scales)")
 
 
 class ZeroLionBridge(ZeroAdamBridge):

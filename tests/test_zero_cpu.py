@@ -50,6 +50,31 @@ def test_one_round_without_peers():
     assert FlatLayout(SIZES, 1).rounds == 1
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+@pytest.mark.parametrize("rounds", [None, 1, 4])
+@pytest.mark.parametrize("unit,padded", [(1, False), (1, True), (ALIGN, True)])
+def test_shard_runs_scatter_and_gather_round_trip(world, rounds, unit, padded):
+    """The checkpoint mapping: per-parameter arrays (padded to whole 128-element blocks for FP8 codes, one
+    entry per block for FP8 scales) scattered into every rank's shard by ``shard_runs`` and gathered back
+    are unchanged, and every entry of every parameter lands in exactly one shard."""
+    L = FlatLayout(SIZES, world, rounds)
+    lengths = [(-(-n // ALIGN) * ALIGN if padded else n) // unit for n in SIZES]
+    rng = np.random.default_rng(world * 100 + (rounds or 0))
+    full = [rng.integers(1, 1 << 30, n) for n in lengths]
+    shards = [np.zeros(L.shard_numel // unit, np.int64) for _ in range(world)]
+    hits = [np.zeros(n, np.int64) for n in lengths]
+    for r in range(world):
+        for index, p_lo, s_lo, length in L.shard_runs(r, unit, padded):
+            shards[r][s_lo:s_lo + length] = full[index][p_lo:p_lo + length]
+            hits[index][p_lo:p_lo + length] += 1
+    assert all((h == 1).all() for h in hits)
+    back = [np.zeros(n, np.int64) for n in lengths]
+    for r in range(world):
+        for index, p_lo, s_lo, length in L.shard_runs(r, unit, padded):
+            back[index][p_lo:p_lo + length] = shards[r][s_lo:s_lo + length]
+    assert all((a == b).all() for a, b in zip(full, back))
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

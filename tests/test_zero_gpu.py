@@ -33,13 +33,15 @@ def _grads(step, device):
     return [(torch.randn(s, generator=g) * 1e-3).to(device, torch.bfloat16) for s in SHAPES]
 
 
-def _reference(algo, precision, steps, device):
+def _reference(algo, precision, steps, device, clip=None):
     params = _params(device)
     cls = ab.LionBridge if algo == "lion" else ab.AdamBridge
     opt = cls(params, lr=1e-3, precision=precision, small_param_threshold=0, seed=3)
     for step in range(1, steps + 1):
         for p, g in zip(params, _grads(step, device)):
             p.grad = g
+        if clip is not None:
+            opt.clip_grad_norm_(clip)
         opt.step()
     torch.cuda.synchronize()
     out = [p.detach().clone() for p in params], [m.clone() for m in opt.master_params()]
@@ -69,7 +71,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, algo, precision, steps, out_dir, gather):
+def _rank(rank, world, port, algo, precision, steps, out_dir, gather, clip=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
@@ -82,6 +84,8 @@ def _rank(rank, world, port, algo, precision, steps, out_dir, gather):
         for step in range(1, steps + 1):
             for p, g in zip(params, _grads(step, f"cuda:{rank}")):
                 p.grad = g
+            if clip is not None:
+                opt.clip_grad_norm_(clip)
             opt.step()
         torch.cuda.synchronize()
         with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
@@ -105,3 +109,159 @@ def test_zero_two_gpus_equals_unsharded(tmp_path, algo, precision, gather):
         got = pickle.load(open(tmp_path / f"rank{r}.pkl", "rb"))
         for g, w in zip(got, want_w):
             assert torch.equal(g, w.cpu())
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("gather", ["nccl", "p2p"])
+def test_zero_two_gpus_clip_equals_unsharded(tmp_path, gather):
+    """clip_grad_norm_ on the sharded, reduced gradients (per-parameter sums of squares all-reduced) then
+    step() == the unsharded AdamBridge's clip_grad_norm_ + step(), on every rank."""
+    steps = 3
+    want_w, _ = _reference("adamw", "bf16", steps, "cuda:0", clip=2e-3)
+    mp.start_processes(_rank, args=(2, _free_port(), "adamw", "bf16", steps, str(tmp_path), gather, 2e-3), nprocs=2,
+                       start_method="spawn", join=True)
+    for r in range(2):
+        got = pickle.load(open(tmp_path / f"rank{r}.pkl", "rb"))
+        for g, w in zip(got, want_w):
+            assert torch.equal(g, w.cpu())
+
+
+# ---------------------------------------------------------------------------------------------- checkpoints
+
+def _bits(t: torch.Tensor) -> torch.Tensor:
+    t = t.detach().cpu().reshape(-1)
+    return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
+
+
+def _assert_same_state(a: dict, b: dict) -> None:
+    """Two checkpoints in the AdamBridge format hold the same bits for every parameter."""
+    assert sorted(a["state"]) == sorted(b["state"])
+    for i in a["state"]:
+        sa, sb = a["state"][i], b["state"][i]
+        assert int(sa["step"]) == int(sb["step"])
+        for key in ("master", "exp_avg", "exp_avg_sq"):
+            if key not in sa:
+                assert key not in sb
+                continue
+            xa, xb = sa[key], sb[key]
+            if isinstance(xa, torch.Tensor):
+                assert torch.equal(_bits(xa), _bits(xb)), (i, key)
+                continue
+            assert {k for k in xa if isinstance(xa[k], torch.Tensor)} == {k for k in xb if isinstance(xb[k], torch.Tensor)}
+            for k, v in xa.items():
+                if isinstance(v, torch.Tensor):
+                    assert torch.equal(_bits(v), _bits(xb[k])), (i, key, k)
+                else:
+                    assert v == xb[k], (i, key, k)
+
+
+def _run_steps(opt, params, first, last, device):
+    for step in range(first, last + 1):
+        for p, g in zip(params, _grads(step, device)):
+            p.grad = g
+        opt.step()
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("algo,precision,master", [("adamw", "bf16", "fp32"), ("adamw", "fp8", "fp24"),
+                                                    ("adamw", "fp32", "fp32"), ("lion", "fp8", "fp32")])
+def test_zero_checkpoint_is_the_adambridge_checkpoint(algo, precision, master):
+    """A world-1 ZeRO optimizer (3 rounds, so tensors are cut into pieces) gathers exactly the checkpoint the
+    unsharded AdamBridge writes; loading that checkpoint into a fresh ZeRO optimizer and continuing equals the
+    AdamBridge continuing."""
+    cls_a = ab.LionBridge if algo == "lion" else ab.AdamBridge
+    cls_z = ZeroLionBridge if algo == "lion" else ZeroAdamBridge
+    kw = dict(lr=1e-3, precision=precision, master_precision=master, seed=3)
+    pa = _params("cuda")
+    oa = cls_a(pa, small_param_threshold=0, **kw)
+    _run_steps(oa, pa, 1, 3, "cuda")
+    pz = _params("cuda")
+    oz = cls_z(pz, rounds=3, **kw)
+    _run_steps(oz, pz, 1, 3, "cuda")
+    sd_a, sd_z = oa.state_dict(), oz.state_dict()
+    _assert_same_state(sd_a, sd_z)
+    assert sd_z["adambridge"] == sd_a["adambridge"]
+
+    # resume: fresh ZeRO optimizer over the AdamBridge's current weights, loaded from its checkpoint
+    pr = [torch.nn.Parameter(p.detach().clone()) for p in pa]
+    orr = cls_z(pr, rounds=2, **kw)
+    orr.load_state_dict(sd_a)
+    _run_steps(oa, pa, 4, 5, "cuda")
+    _run_steps(orr, pr, 4, 5, "cuda")
+    for x, y in zip(pa, pr):
+        assert torch.equal(x, y)
+    _assert_same_state(oa.state_dict(), orr.state_dict())
+    oa.close()
+
+
+def test_zero_checkpoint_converts_precision_and_checks_shapes():
+    pa = _params("cuda")
+    oa = ab.AdamBridge(pa, lr=1e-3, precision="fp32", small_param_threshold=0, seed=3)
+    _run_steps(oa, pa, 1, 2, "cuda")
+    sd = oa.state_dict()
+    oz = ZeroAdamBridge(_params("cuda"), lr=1e-3, precision="bf16", seed=3)
+    oz.load_state_dict(sd)
+    got = oz.state_dict()
+    for i, st in sd["state"].items():
+        want = st["exp_avg"]["data"].to(torch.bfloat16)
+        assert torch.equal(got["state"][i]["exp_avg"]["data"], want.cpu())
+    bad = {"state": {i: dict(st) for i, st in sd["state"].items()}, "param_groups": sd["param_groups"]}
+    bad["state"][3]["exp_avg"] = {"precision": "fp32", "data": torch.zeros(7)}
+    before = oz.state_dict()
+    with pytest.raises(ValueError, match="7 elements"):
+        oz.load_state_dict(bad)
+    _assert_same_state(before, oz.state_dict())      # a rejected checkpoint changes nothing
+    partial = {"state": {0: sd["state"][0]}, "param_groups": sd["param_groups"]}
+    with pytest.raises(ValueError, match="every parameter"):
+        oz.load_state_dict(partial)
+    oa.close()
+
+
+def _ckpt_rank(rank, world, port, out_dir, gather, saved_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        dev = f"cuda:{rank}"
+        params = _params(dev)
+        opt = ZeroAdamBridge(params, lr=1e-3, precision="fp8", seed=3, rounds=2, gather=gather)
+        _run_steps(opt, params, 1, 3, dev)
+        sd = opt.state_dict(rank0_only=True)
+        if rank == 0:
+            torch.save(sd, os.path.join(out_dir, "gathered.pt"))
+        else:
+            assert sd["state"] == {}
+        # resume from the unsharded optimizer's checkpoint on fresh weights, and continue
+        saved = torch.load(saved_path, map_location="cpu", weights_only=False)
+        fresh = [torch.nn.Parameter(w.to(dev)) for w in saved["weights"]]
+        opt2 = ZeroAdamBridge(fresh, lr=1e-3, precision="fp8", seed=3, rounds=3, gather=gather)
+        opt2.load_state_dict(saved["optimizer"])
+        _run_steps(opt2, fresh, 4, 5, dev)
+        with open(os.path.join(out_dir, f"resumed{rank}.pkl"), "wb") as f:
+            pickle.dump([p.detach().cpu() for p in fresh], f)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("gather", ["nccl", "p2p"])
+def test_zero_two_gpus_checkpoint_gather_and_resume(tmp_path, gather):
+    """2 ranks: the gathered checkpoint equals the unsharded AdamBridge's; an unsharded checkpoint loaded into
+    2 ranks and continued equals the unsharded optimizer continuing."""
+    pa = _params("cuda:0")
+    oa = ab.AdamBridge(pa, lr=1e-3, precision="fp8", small_param_threshold=0, seed=3)
+    _run_steps(oa, pa, 1, 3, "cuda:0")
+    sd_a = oa.state_dict()
+    saved_path = str(tmp_path / "unsharded.pt")
+    torch.save({"optimizer": sd_a, "weights": [p.detach().cpu() for p in pa]}, saved_path)
+    mp.start_processes(_ckpt_rank, args=(2, _free_port(), str(tmp_path), gather, saved_path), nprocs=2,
+                       start_method="spawn", join=True)
+    _assert_same_state(sd_a, torch.load(tmp_path / "gathered.pt", weights_only=False))
+    _run_steps(oa, pa, 4, 5, "cuda:0")
+    for r in range(2):
+        got = pickle.load(open(tmp_path / f"resumed{r}.pkl", "rb"))
+        for g, w in zip(got, pa):
+            assert torch.equal(g, w.detach().cpu())
+    oa.close()
