@@ -19,6 +19,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "../../include/abx.h"
@@ -28,6 +29,7 @@
 namespace abx {
 int set_error(const char* what, cudaError_t e);   // abx_kernels.cu
 extern std::atomic<uint64_t> g_launches;
+extern thread_local char g_err[512];
 }
 
 namespace abx_clip {
@@ -283,6 +285,116 @@ ABX_API int abx_clip_coef(void* stream, const abx_tensor* grads, int32_t n, floa
     for (int32_t i = 1; i < n; ++i)
         if (grads[i].dtype != dtype) return ABX_E_G_DTYPE;   // torch rounds the norms in one dtype
     int rc = abx_grad_sq_norms(stream, grads, n, sq, workspace, workspace_bytes);
+    if (rc) return rc;
+    return abx_clip_coef_from_sq(stream, sq, n, dtype, max_norm, norms, total_coef);
+}
+
+// ---- abx_clip_coef_noalloc: abx_clip_coef with its scratch in this library's own device memory ----
+//
+// The per-tile partial sums live in a file-scope __device__ array of kNoAllocTiles floats (2 MiB per
+// device, enough for 524,288 tiles of 16384 elements: about 8.59e9 gradient elements), so a call
+// needs no caller workspace and allocates nothing, on the device or the host.  The array's device
+// address is looked up once per device, with that device current, on the first call there (this is
+// also when the module's device code is loaded): make that first call before any stream capture.
+// Every partial that a call reads was written earlier in the same call, so nothing needs to start at
+// zero.  All calls on one device share the array: calls whose work overlaps on the device (issued
+// to two streams, or from two host threads without ordering) race on it.
+
+constexpr int64_t kNoAllocTiles = int64_t(1) << 19;
+constexpr int kNoAllocDevices = 64;
+
+__device__ __align__(256) float g_noalloc_partials[kNoAllocTiles];
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_addr[kNoAllocDevices];
+
+static int noalloc_scratch(float** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return abx::set_error("abx_clip_coef_noalloc: cudaGetDevice", e);
+    if (dev < 0 || dev >= kNoAllocDevices)
+        return abx::set_error("abx_clip_coef_noalloc: device index out of range", cudaErrorInvalidDevice);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        if (e != cudaSuccess) return abx::set_error("abx_clip_coef_noalloc: cudaGetSymbolAddress", e);
+        g_noalloc_addr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return ABX_OK;
+}
+
+// The launches of abx_grad_sq_norms, with the tile offsets kept as a running count (no host buffers).
+static int sq_norms_into(cudaStream_t st, const abx_tensor* grads, int32_t n, float* sq, float* partial)
+{
+    int64_t next = 0;
+    for (int32_t b = 0; b < n; b += kMaxTensors) {
+        const int cnt = n - b < kMaxTensors ? n - b : kMaxTensors;
+        PartialArgs pa;
+        std::memset(&pa, 0, sizeof pa);
+        ReduceArgs ra;
+        std::memset(&ra, 0, sizeof ra);
+        const int64_t t0 = next;
+        for (int j = 0; j < cnt; ++j) {
+            const abx_tensor& g = grads[b + j];
+            const int64_t tiles = g.n > 0 ? tiles_of(g.n) : 0;
+            pa.t[j] = NTensor{g.data, g.n, next, g.dtype == ABX_DT_BF16, (reinterpret_cast<uintptr_t>(g.data) % 16) == 0};
+            ra.tile_begin[j] = next;
+            ra.tiles[j] = tiles;
+            next += tiles;
+        }
+        pa.ntensor = cnt;
+        pa.first_tile = t0;
+        pa.total_tiles = next - t0;
+        pa.partial = partial;
+        if (pa.total_tiles > 0) {
+            norm_partials<<<grid_of(pa.total_tiles), kThreads, 0, st>>>(pa);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return abx::set_error("norm_partials launch", e);
+            abx::g_launches.fetch_add(1, std::memory_order_relaxed);
+        }
+        ra.ntensor = cnt;
+        ra.first = b;
+        ra.partial = partial;
+        ra.sq = sq;
+        norm_reduce<<<cnt, kThreads, 0, st>>>(ra);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return abx::set_error("norm_reduce launch", e);
+        abx::g_launches.fetch_add(1, std::memory_order_relaxed);
+    }
+    return ABX_OK;
+}
+
+ABX_API int abx_clip_coef_noalloc(void* stream, const abx_tensor* grads, int32_t n, float max_norm, float* sq,
+                                  float* norms, float* total_coef)
+{
+    if (n <= 0 || !grads || !sq || !total_coef) return ABX_E_ARG;
+    const int32_t dtype = grads[0].dtype;
+    int64_t tiles = 0;
+    for (int32_t i = 0; i < n; ++i) {
+        const abx_tensor& g = grads[i];
+        if (g.n < 0) return ABX_E_ARG;
+        if (g.n > 0 && !g.data) return ABX_E_NULL_PTR;
+        if (g.dtype != ABX_DT_F32 && g.dtype != ABX_DT_BF16) return ABX_E_G_DTYPE;
+        if (g.dtype != dtype) return ABX_E_G_DTYPE;           // torch rounds the norms in one dtype
+        if (reinterpret_cast<uintptr_t>(g.data) % (g.dtype == ABX_DT_BF16 ? 2 : 4)) return ABX_E_ALIGN;
+        const int64_t t = g.n > 0 ? tiles_of(g.n) : 0;
+        if (t > kNoAllocTiles - tiles) {
+            snprintf(abx::g_err, sizeof abx::g_err,
+                     "abx_clip_coef_noalloc: the gradients need more than %lld norm tiles of %d elements "
+                     "(the static scratch); use abx_clip_coef with a workspace",
+                     (long long)kNoAllocTiles, kNormTile);
+            return ABX_E_SCRATCH;
+        }
+        tiles += t;
+    }
+    if (reinterpret_cast<uintptr_t>(sq) % 4 || reinterpret_cast<uintptr_t>(total_coef) % 4) return ABX_E_ALIGN;
+    float* partial = nullptr;
+    int rc = noalloc_scratch(&partial);
+    if (rc) return rc;
+    rc = sq_norms_into(static_cast<cudaStream_t>(stream), grads, n, sq, partial);
     if (rc) return rc;
     return abx_clip_coef_from_sq(stream, sq, n, dtype, max_norm, norms, total_coef);
 }

@@ -46,6 +46,7 @@ ERRORS = {
     -7: "FP8 moments without scales", -8: "segment without a group", -9: "too many work items",
     -10: "out of memory", -11: "bad element offset", -12: "unknown algorithm", -13: "unknown master dtype",
     -20: "CUDA error", -21: "misaligned buffer", -22: "unknown SIMD level",
+    -23: "gradients exceed the static norm scratch",
 }
 
 _MASK64 = (1 << 64) - 1
@@ -228,6 +229,9 @@ class NativeKernels:
         lib.abx_clip_coef.restype = ctypes.c_int
         lib.abx_clip_coef.argtypes = [ctypes.c_void_p, tens, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+        lib.abx_clip_coef_noalloc.restype = ctypes.c_int
+        lib.abx_clip_coef_noalloc.argtypes = [ctypes.c_void_p, tens, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_void_p]
         self._lib = lib
 
     # -- rounding pattern ----------------------------------------------------
@@ -265,7 +269,7 @@ class NativeKernels:
 
     def _check(self, rc: int, what: str) -> None:
         if rc != 0:
-            detail = self._lib.abx_last_error().decode() if rc in (-20, -21) else ERRORS.get(rc, "")
+            detail = self._lib.abx_last_error().decode() if rc in (-20, -21, -23) else ERRORS.get(rc, "")
             raise RuntimeError(f"{what} rejected the update (code {rc}: {detail})")
 
     def multi_step(self, stream, segments: ctypes.Array, max_ctas: int = 0, g_scale: torch.Tensor | None = None) -> None:
@@ -337,6 +341,22 @@ class NativeKernels:
                                              float(max_norm), None if norms is None else norms.data_ptr(),
                                              total_coef.data_ptr())
         self._check(rc, "abx_clip_coef_from_sq")
+
+    def clip_coef(self, stream, arr: ctypes.Array, n: int, max_norm: float, sq: torch.Tensor,
+                  norms: torch.Tensor | None, total_coef: torch.Tensor, workspace: torch.Tensor) -> None:
+        """abx_clip_coef: sums of squares, norms, total norm and coefficient, with a caller workspace."""
+        rc = self._lib.abx_clip_coef(_stream_handle(stream), arr, n, float(max_norm), sq.data_ptr(),
+                                     None if norms is None else norms.data_ptr(), total_coef.data_ptr(),
+                                     workspace.data_ptr(), workspace.numel() * workspace.element_size())
+        self._check(rc, "abx_clip_coef")
+
+    def clip_coef_noalloc(self, stream, arr: ctypes.Array, n: int, max_norm: float, sq: torch.Tensor,
+                          norms: torch.Tensor | None, total_coef: torch.Tensor) -> None:
+        """abx_clip_coef_noalloc: the same results with the library's static device scratch (no workspace,
+        nothing allocated; calls that overlap on one device race on the scratch)."""
+        rc = self._lib.abx_clip_coef_noalloc(_stream_handle(stream), arr, n, float(max_norm), sq.data_ptr(),
+                                             None if norms is None else norms.data_ptr(), total_coef.data_ptr())
+        self._check(rc, "abx_clip_coef_noalloc")
 
     def pipeline_status(self) -> int:
         """Nonzero if an update kernel's bounded pipeline wait gave up since the last call (then cleared).

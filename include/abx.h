@@ -73,6 +73,7 @@ enum { ABX_SIMD_SCALAR = 0, ABX_SIMD_AVX2 = 1, ABX_SIMD_AVX512 = 2, ABX_SIMD_NEO
 #define ABX_E_CUDA           -20   /* a CUDA runtime call failed; see abx_last_error() */
 #define ABX_E_ALIGN          -21   /* a buffer is not aligned to its element size */
 #define ABX_E_SIMD_LEVEL     -22   /* unknown SIMD level */
+#define ABX_E_SCRATCH        -23   /* more gradient than abx_clip_coef_noalloc's static scratch covers */
 
 /* Per-step coefficients (adambridge_hparams, adambridge_kernels.c:77-88). */
 typedef struct abx_hparams {
@@ -213,6 +214,22 @@ int abx_clip_coef_from_sq(void* stream, const float* sq, int32_t n, int32_t dtyp
 int abx_clip_coef(void* stream, const abx_tensor* grads, int32_t n, float max_norm, float* sq, float* norms,
                   float* total_coef, void* workspace, size_t workspace_bytes);
 
+/* abx_clip_coef without a caller workspace.  No counterpart in the reference (adambridge has no
+ * device-side norm: its callers run torch.nn.utils.clip_grad_norm_).  The per-tile partial sums
+ * live in a static device array inside this library (2 MiB per device), so the call allocates
+ * nothing: no cudaMalloc, no caller buffer beyond its outputs sq, norms (may be NULL) and
+ * total_coef, whose meaning is abx_clip_coef's.
+ *   Limit: the gradients' 16384-element tiles, the sum of ceil(n_i / 16384), must number at most
+ *   524,288 (about 8.59e9 elements); more is rejected before anything runs, with ABX_E_SCRATCH
+ *   and a message in abx_last_error().
+ *   Set-up: the first call on each device looks up the array's address (cudaGetSymbolAddress,
+ *   with that device current); make that first call before any stream capture.
+ *   Nothing needs to start at zero: every partial a call reads was written earlier in that call.
+ *   All calls on one device share the array: calls whose work overlaps on the device (two
+ *   streams, or two host threads without ordering between them) race on it. */
+int abx_clip_coef_noalloc(void* stream, const abx_tensor* grads, int32_t n, float max_norm, float* sq, float* norms,
+                          float* total_coef);
+
 /* Kernel launches this library has made in this process, all threads and devices. */
 uint64_t abx_launch_count(void);
 
@@ -223,7 +240,7 @@ uint64_t abx_launch_count(void);
  * incomplete) and clears it, or ABX_E_CUDA.  Synchronizes with the device. */
 int abx_pipeline_status(void);
 
-/* Message of the last ABX_E_CUDA / ABX_E_ALIGN error on this thread (never NULL). */
+/* Message of the last ABX_E_CUDA / ABX_E_ALIGN / ABX_E_SCRATCH error on this thread (never NULL). */
 const char* abx_last_error(void);
 
 #ifdef __cplusplus

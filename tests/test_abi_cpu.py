@@ -132,6 +132,22 @@ def test_fused_adamw_argument_codes(kernels):
     assert f(0x10, 0x20, 1, 0x30, 0x40, 1, None, 2, 8, 0, ctypes.byref(hp), None) == -6
 
 
+def test_clip_noalloc_limit_rejected_before_any_cuda_call(kernels):
+    """abx_clip_coef_noalloc's static scratch holds 524,288 norm tiles of 16384 elements: gradients needing one
+    tile more get ABX_E_SCRATCH (-23) and a message, from host checks made before any CUDA call (here, with no
+    GPU, a CUDA call would return -20 instead).  The pointers are never dereferenced."""
+    from adambridge_b200 import native
+    arr = (native.Tensor * 2)()
+    arr[0] = native.Tensor(0x1000, 16384 * 524_288, native.DT_BF16, 0)
+    arr[1] = native.Tensor(0x2000, 1, native.DT_BF16, 0)
+    f = kernels._lib.abx_clip_coef_noalloc
+    assert f(None, arr, 2, 1.0, 0x3000, None, 0x4000) == -23
+    assert b"static scratch" in kernels._lib.abx_last_error()
+    assert f(None, arr, 0, 1.0, 0x3000, None, 0x4000) == -1
+    arr[1] = native.Tensor(0x2000, 1, native.DT_F32, 0)
+    assert f(None, arr, 2, 1.0, 0x3000, None, 0x4000) == -3      # one dtype for all gradients
+
+
 def test_product_loader_fails_loudly_without_library(tmp_path, monkeypatch):
     """No fallback: a missing library raises instead of switching to another implementation."""
     from adambridge_b200 import native
