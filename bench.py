@@ -30,6 +30,11 @@ sys.path.insert(0, str(ROOT))
 LLAMA7B = dict(hidden=4096, layers=32, mlp=11008, vocab=32000, kv=4096)
 BYTES_PER_PARAM = {("adamw", "bf16"): 20, ("adamw", "fp32"): 28, ("adamw", "fp8"): 16.125,
                    ("lion", "bf16"): 16, ("lion", "fp32"): 20, ("lion", "fp8"): 14.0625}
+# DRAM bytes (read + write) per parameter of the update kernel, from one ncu capture of the small Llama case
+# (1 layer, vocab 8000: 267,923,456 parameters); the traffic of a launch grows with its parameters, so the
+# full-size figure is this times the parameters a step updates.  Summaries: profiles/update_kernel_adamw_*.md
+MEASURED_DRAM_BYTES_PER_PARAM = {("adamw", "bf16"): (2.679314e9 + 2.621452e9) / 267923456,
+                                 ("adamw", "fp8"): (2.160244e9 + 2.103694e9) / 267923456}
 
 
 def llama_shapes(hidden, layers, mlp, vocab, kv, tied=False):
@@ -312,7 +317,11 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                    "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None,
                    "l2": "no flush: each step streams %.1f GB >> 126 MB L2" % (bpp * shard_params / 1e9)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4),
+                     "traffic": (round(MEASURED_DRAM_BYTES_PER_PARAM[(algo, prec)] * shard_params)
+                                 if (algo, prec) in MEASURED_DRAM_BYTES_PER_PARAM else None),
+                     "traffic_basis": "dram__bytes_read.sum + dram__bytes_write.sum per parameter from ncu on the "
+                                      "1-layer case, times the parameters of one step (all of its launches)",
                      "basis": f"{bpp} B/param x {shard_params:,} params per rank per step / update-kernel time "
                               f"{kernel_ms_max:.3f} ms (CUDA events on the update stream, {n_launches_trace // args.steps} "
                               f"multi-segment calls per step); peak = MEASURED_PEAKS.json hbm_gbs (of measured)"},
