@@ -33,6 +33,9 @@ BYTES_PER_PARAM = {("adamw", "bf16"): 20, ("adamw", "fp32"): 28, ("adamw", "fp8"
 # DRAM bytes (read + write) per parameter of the update kernel, from one ncu capture of the small Llama case
 # (1 layer, vocab 8000: 267,923,456 parameters); the traffic of a launch grows with its parameters, so the
 # full-size figure is this times the parameters a step updates.  Summaries: profiles/update_kernel_adamw_*.md
+# NVLink 5 peer copy measured on this pool's B200s, per direction per GPU (900 GB/s nominal): the denominator for a
+# kernel bound by its stores into the peers' memory
+NVLINK_PEER_GBS = 770.0
 MEASURED_DRAM_BYTES_PER_PARAM = {("adamw", "bf16"): (2.679314e9 + 2.621452e9) / 267923456,
                                  ("adamw", "fp8"): (2.160244e9 + 2.103694e9) / 267923456}
 
@@ -302,7 +305,21 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     if pk.exists():
         peaks = json.loads(pk.read_text())
     peak = peaks.get("hbm_gbs", 6650.0)
-    achieved = bpp * shard_params / (kernel_ms_max / 1e3) / 1e9
+    peak_note = "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks else "6650 GB/s (of fallback)"
+    fused_gather = world > 1 and opt._peer_deltas is not None
+    hbm_bytes = bpp * shard_params
+    nvl_bytes = 0
+    if fused_gather:
+        # the kernel also stores its new bf16 weights into the world - 1 peers (NVLink egress) and receives the
+        # peers' (NVLink ingress, written into this GPU's HBM): per direction, (world - 1) x its shard
+        nvl_bytes = (world - 1) * shard_params * 2
+        hbm_bytes += nvl_bytes
+    bound = "nvlink" if nvl_bytes / NVLINK_PEER_GBS > hbm_bytes / peak else "hbm"
+    if bound == "nvlink":
+        achieved = nvl_bytes / (kernel_ms_max / 1e3) / 1e9
+        peak, peak_note = NVLINK_PEER_GBS, f"{NVLINK_PEER_GBS:.0f} GB/s peer copy per direction (of measured on this pool)"
+    else:
+        achieved = hbm_bytes / (kernel_ms_max / 1e3) / 1e9
     line = {
         "metric": "fused step Gparams/s and % of HBM roofline (7B, bf16 moments)" if (algo, prec) == ("adamw", "bf16")
         else f"fused step Gparams/s ({algo}, {prec} moments)",
@@ -316,15 +333,17 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                    "parallelism": f"zero1-dp{world}", "rounds": L.rounds, "max_ctas": args.max_ctas,
                    "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None,
                    "l2": "no flush: each step streams %.1f GB >> 126 MB L2" % (bpp * shard_params / 1e9)},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
                      "traffic": (round(MEASURED_DRAM_BYTES_PER_PARAM[(algo, prec)] * shard_params)
                                  if (algo, prec) in MEASURED_DRAM_BYTES_PER_PARAM else None),
                      "traffic_basis": "dram__bytes_read.sum + dram__bytes_write.sum per parameter from ncu on the "
                                       "1-layer case, times the parameters of one step (all of its launches)",
-                     "basis": f"{bpp} B/param x {shard_params:,} params per rank per step / update-kernel time "
-                              f"{kernel_ms_max:.3f} ms (CUDA events on the update stream, {n_launches_trace // args.steps} "
-                              f"multi-segment calls per step); peak = MEASURED_PEAKS.json hbm_gbs (of measured)"},
+                     "basis": (f"{bpp} B/param x {shard_params:,} params per rank per step"
+                               + (f" + {nvl_bytes / 1e9:.2f} GB of peers' weights received" if fused_gather else "")
+                               + (f"; NVLink: {nvl_bytes / 1e9:.2f} GB per direction per rank" if fused_gather else "")
+                               + f" / update-kernel time {kernel_ms_max:.3f} ms (CUDA events on the update stream, "
+                               f"{n_launches_trace // args.steps} multi-segment calls per step); peak = {peak_note}")},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "e2e": e2e,
