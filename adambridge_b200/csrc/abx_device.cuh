@@ -31,6 +31,26 @@ __device__ __forceinline__ uint32_t hash32(uint32_t x)
     return x ^ (x >> 16);
 }
 
+// The hash words of elements idx0 .. idx0+3 of one stream.  When idx0 is a multiple of 4 (a
+// segment whose offset is), the inputs (idx0 + k) ^ seed = X ^ k differ only in their two low
+// bits, so the first xor-shift is shared: (X ^ k) ^ ((X ^ k) >> 16) = (X ^ (X >> 16)) ^ k.
+__device__ __forceinline__ void hash4(uint32_t idx0, uint32_t seed, uint32_t (&r)[4])
+{
+    if ((idx0 & 3U) == 0) {
+        const uint32_t x0 = idx0 ^ seed;
+        const uint32_t s = x0 ^ (x0 >> 16);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t x = (s ^ (uint32_t)k) * 0x7feb352dU;
+            x = (x ^ (x >> 15)) * 0x846ca68bU;
+            r[k] = x ^ (x >> 16);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) r[k] = hash32((idx0 + (uint32_t)k) ^ seed);
+    }
+}
+
 // bf16 bits of x (in the high half), nearest-even; NaN quieted (csrc:108-112).
 __device__ __forceinline__ uint32_t bf16_rne(uint32_t b)
 {
@@ -196,6 +216,15 @@ __device__ __forceinline__ f2x mul2(f2x a, f2x b)
     return d;
 }
 
+// x / s for a pair, correctly rounded, by Markstein's correction (see div_by_scale below):
+// Y = (RN(1/s), RN(1/s)), NS = (-s, -s).  Valid for the same range of s and x; signed x gives the
+// negated quotient of |x| (every step rounds symmetrically) except that -0 comes out +0.
+__device__ __forceinline__ f2x div2(f2x X, f2x Y, f2x NS)
+{
+    const f2x Q0 = mul2(X, Y);
+    return fma2(fma2(Q0, NS, X), Y, Q0);
+}
+
 // The update's coefficients as pairs (both lanes equal).
 struct Coef2 {
     f2x b1, b2, omb1, omb2, decay, nstep, isbc2, eps;
@@ -261,21 +290,19 @@ __device__ __noinline__ uint32_t enc4_fp8_slow(float x0, float x1, float x2, flo
     return enc4_fp8<E4M3, SR>(x, r);
 }
 
-// 4 floats -> 4 codes with the sign handled by the converter: the stochastic truncation only touches
-// significand bits (a carry out of them ends at the exponent, never in the sign bit, for any non-NaN
-// value), and cvt.rn.satfinite is symmetric in the sign, so sign | code(|t|) == cvt(t).  A NaN
-// input (rare) falls back to enc4_fp8, which gives the reference's NaN code.
+// 4 non-NaN floats -> 4 codes (byte k = element k), the sign handled by the converter: the
+// stochastic truncation only touches significand bits (a carry out of them ends in the exponent,
+// never in the sign bit, for any non-NaN value), and cvt.rn.satfinite is symmetric in the sign,
+// so sign | code(|t|) == cvt(t).  Callers route groups that may hold a NaN to enc4_fp8.
 template <bool E4M3, bool SR>
-__device__ __forceinline__ uint32_t enc4_signed(const float (&x)[4], const uint32_t (&r)[4])
+__device__ __forceinline__ uint32_t enc4_plain(const float (&x)[4], const uint32_t (&r)[4])
 {
     constexpr uint32_t low = (1U << (23 - (E4M3 ? 3 : 2))) - 1U;
     float a[4];
-    bool nan = false;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t b = f2u(x[k]);
         a[k] = u2f(SR ? ((b + (r[k] & low)) & ~low) : b);
-        nan |= (b & 0x7fffffffU) > 0x7f800000U;
     }
     uint16_t c01, c23;
     if (E4M3) {
@@ -285,9 +312,7 @@ __device__ __forceinline__ uint32_t enc4_signed(const float (&x)[4], const uint3
         asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c01) : "f"(a[1]), "f"(a[0]));
         asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(a[3]), "f"(a[2]));
     }
-    const uint32_t w = (uint32_t)c01 | ((uint32_t)c23 << 16);
-    if (__builtin_expect(nan, 0)) return enc4_fp8_slow<E4M3, SR>(x[0], x[1], x[2], x[3], r[0], r[1], r[2], r[3]);
-    return w;
+    return (uint32_t)c01 | ((uint32_t)c23 << 16);
 }
 
 // ---- division by a block scale -------------------------------------------------------

@@ -304,11 +304,11 @@ template <int PT, bool SR>
 __device__ __forceinline__ void store_master4(const KSeg& S, int64_t i0, int cnt, float (&p)[4])
 {
     if constexpr (PT == ABX_DT_F24) {
-        uint32_t b[4];
+        uint32_t b[4], r[4] = {0U, 0U, 0U, 0U};
+        if (SR) hash4(S.off32 + (uint32_t)i0, S.s_p, r);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const uint32_t r = SR ? hash32((S.off32 + (uint32_t)(i0 + k)) ^ S.s_p) : 0U;
-            b[k] = f24_bits(f2u(p[k]), SR, r);
+            b[k] = f24_bits(f2u(p[k]), SR, r[k]);
             p[k] = u2f(b[k]);
         }
         // lo plane: byte 1 of each word, packed in element order
@@ -359,9 +359,10 @@ __device__ __forceinline__ void store_moment4(void* base, int64_t i0, int cnt, b
     if constexpr (MV == ABX_DT_BF16) {
         uint32_t w0, w1;
         if constexpr (SR) {
-            uint32_t b[4];
+            uint32_t b[4], r[4];
+            hash4(idx0, seed, r);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) b[k] = f2u(x[k]) + (hash32((idx0 + (uint32_t)k) ^ seed) & 0xffffU);
+            for (int k = 0; k < 4; ++k) b[k] = f2u(x[k]) + (r[k] & 0xffffU);
             w0 = pack_hi16(b[0], b[1]);
             w1 = pack_hi16(b[2], b[3]);
         } else {
@@ -658,23 +659,49 @@ __device__ __forceinline__ float absmax4(const float (&x)[4])
     return fmaxf(fmaxf(fmaxf(fmaxf(0.0f, fabsf(x[0])), fabsf(x[1])), fabsf(x[2])), fabsf(x[3]));
 }
 
-// Codes of x[k] / s for a whole group of 4 (fast path of encode4).
-template <bool E4M3, bool SR>
-__device__ __forceinline__ uint32_t fast_encode4(const float (&x)[4], float s, uint32_t idx0, uint32_t seed)
+// Codes of a whole group of 4 (the fast path of encode4), for a block scale s (warp-uniform, so the
+// branches are too).  In the common case -- s in Markstein's range -- the quotients are packed pairs.
+// m: signed; a NaN m (from a NaN gradient; the block maximum skips it) is caught by a NaN sum of the
+// group and encoded by the exact out-of-line path.  -0 keeps its sign (copysign after the division).
+template <bool SR>
+__device__ __forceinline__ uint32_t fast_encode_m4(const float (&x)[4], float s, uint32_t idx0, uint32_t seed)
 {
+    uint32_t r[4] = {0U, 0U, 0U, 0U};
+    if (SR) hash4(idx0, seed, r);
     float q[4];
     if (__builtin_expect(fast_scale(s), 1)) {
         const float y = __frcp_rn(s);
+        const f2x Y = pk2(y, y), NS = pk2(-s, -s);
+        up2(div2(pk2(x[0], x[1]), Y, NS), q[0], q[1]);
+        up2(div2(pk2(x[2], x[3]), Y, NS), q[2], q[3]);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) q[k] = div_by_scale(x[k], s, y);
+        for (int k = 0; k < 4; ++k) q[k] = copysignf(q[k], x[k]);
+        const float sum = __fadd_rn(__fadd_rn(q[0], q[1]), __fadd_rn(q[2], q[3]));   // finite unless a q is NaN
+        if (__builtin_expect(sum == sum, 1)) return enc4_plain<true, SR>(q, r);
     } else {
         const float4 d = div4_ieee(make_float4(x[0], x[1], x[2], x[3]), s);
         q[0] = d.x; q[1] = d.y; q[2] = d.z; q[3] = d.w;
     }
-    uint32_t r[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) r[k] = SR ? hash32((idx0 + (uint32_t)k) ^ seed) : 0U;
-    return enc4_signed<E4M3, SR>(q, r);
+    return enc4_fp8_slow<true, SR>(q[0], q[1], q[2], q[3], r[0], r[1], r[2], r[3]);
+}
+
+// u = sqrt(max(v, 0)): never NaN and, with s in Markstein's range, finite, so the quotients need no NaN
+// or sign handling; s outside that range (u infinite or tiny) takes the exact out-of-line path.
+template <bool SR>
+__device__ __forceinline__ uint32_t fast_encode_u4(const float (&x)[4], float s, uint32_t idx0, uint32_t seed)
+{
+    uint32_t r[4] = {0U, 0U, 0U, 0U};
+    if (SR) hash4(idx0, seed, r);
+    float q[4];
+    if (__builtin_expect(fast_scale(s), 1)) {
+        const float y = __frcp_rn(s);
+        const f2x Y = pk2(y, y), NS = pk2(-s, -s);
+        up2(div2(pk2(x[0], x[1]), Y, NS), q[0], q[1]);
+        up2(div2(pk2(x[2], x[3]), Y, NS), q[2], q[3]);
+        return enc4_plain<false, SR>(q, r);
+    }
+    const float4 d = div4_ieee(make_float4(x[0], x[1], x[2], x[3]), s);
+    return enc4_fp8_slow<false, SR>(d.x, d.y, d.z, d.w, r[0], r[1], r[2], r[3]);
 }
 
 template <int ALGO, int PT, int GT, bool SR>
@@ -706,7 +733,7 @@ __device__ __forceinline__ void fast_fp8(const KSeg& S, int64_t base, const uint
             store_out4(S, i0, 4, p);
             const float am = warp_max_nonneg(absmax4(mt));
             const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
-            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode4<true, SR>(mt, scm, idx0, S.s_m);
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode_m4<SR>(mt, scm, idx0, S.s_m);
             if (lane == 0) S.m_scale[blk0 + bt] = scm;
         } else {
             const float* swv = reinterpret_cast<const float*>(st + C::OFF_SV + (reinterpret_cast<uintptr_t>(S.v_scale + blk0) & 15));
@@ -730,14 +757,15 @@ __device__ __forceinline__ void fast_fp8(const KSeg& S, int64_t base, const uint
             }
             store_master4<PT, SR>(S, i0, 4, p);
             store_out4(S, i0, 4, p);
+            // u = sqrt(max(v, 0)) (csrc:1000): v >= 0 here, so only a NaN v differs, and fmaxf maps it to 0
 #pragma unroll
-            for (int k = 0; k < 4; ++k) ut[k] = vt[k] > 0.0f ? ut[k] : 0.0f;   // sqrt(max(v, 0)); NaN -> 0
+            for (int k = 0; k < 4; ++k) ut[k] = fmaxf(ut[k], 0.0f);
             const float am = warp_max_nonneg(absmax4(mt));
             const float au = warp_max_nonneg(fmaxf(fmaxf(ut[0], ut[1]), fmaxf(ut[2], ut[3])));
             const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
             const float scu = au > 0.0f ? scale_of<false>(au) : 1.0f;
-            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode4<true, SR>(mt, scm, idx0, S.s_m);
-            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.v) + i0) = fast_encode4<false, SR>(ut, scu, idx0, S.s_v);
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode_m4<SR>(mt, scm, idx0, S.s_m);
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.v) + i0) = fast_encode_u4<SR>(ut, scu, idx0, S.s_v);
             if (lane == 0) { S.m_scale[blk0 + bt] = scm; S.v_scale[blk0 + bt] = scu; }
         }
     }
