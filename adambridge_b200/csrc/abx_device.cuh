@@ -269,15 +269,20 @@ __device__ __forceinline__ void lion2(float& p0, float& p1, float g0, float g1, 
 }
 
 // Block scale absmax / fmax, correctly rounded: the constant reciprocal of fmax with Markstein's
-// correction (exact remainder for amax >= 2^-100), else IEEE division.  amax > 0.
+// correction (exact remainder for finite amax >= 2^-100), else IEEE division (tiny or infinite
+// amax: inf / fmax = inf, as the reference divides).  amax > 0.
+__device__ __forceinline__ float scale_fmt(float amax, float fmax, float y)
+{
+    if (!(amax >= 0x1p-100f && amax <= 0x1p127f)) return __fdiv_rn(amax, fmax);
+    const float q0 = __fmul_rn(amax, y);
+    return __fmaf_rn(__fmaf_rn(-q0, fmax, amax), y, q0);
+}
+
 template <bool E4M3>
 __device__ __forceinline__ float scale_of(float amax)
 {
-    const float fmax = E4M3 ? 448.0f : 57344.0f;
-    const float y = E4M3 ? 0x1.24924ap-9f : 0x1.24924ap-16f;   // RN(1/448), RN(1/57344)
-    if (amax < 0x1p-100f) return __fdiv_rn(amax, fmax);
-    const float q0 = __fmul_rn(amax, y);
-    return __fmaf_rn(__fmaf_rn(-q0, fmax, amax), y, q0);
+    // RN(1/448), RN(1/57344)
+    return E4M3 ? scale_fmt(amax, 448.0f, 0x1.24924ap-9f) : scale_fmt(amax, 57344.0f, 0x1.24924ap-16f);
 }
 
 // Out-of-line copy of enc4_fp8 for the rare groups holding a NaN (kept out of the hot path's code).

@@ -659,18 +659,17 @@ __device__ __forceinline__ float absmax4(const float (&x)[4])
     return fmaxf(fmaxf(fmaxf(fmaxf(0.0f, fabsf(x[0])), fabsf(x[1])), fabsf(x[2])), fabsf(x[3]));
 }
 
-// Codes of a whole group of 4 (the fast path of encode4), for a block scale s (warp-uniform, so the
-// branches are too).  In the common case -- s in Markstein's range -- the quotients are packed pairs.
+// Codes of a whole group of 4 (the fast path of encode4), for a block scale s and y = RN(1/s)
+// (warp-uniform, so the branches are too).  In the common case -- s in Markstein's range -- the quotients are packed pairs.
 // m: signed; a NaN m (from a NaN gradient; the block maximum skips it) is caught by a NaN sum of the
 // group and encoded by the exact out-of-line path.  -0 keeps its sign (copysign after the division).
 template <bool SR>
-__device__ __forceinline__ uint32_t fast_encode_m4(const float (&x)[4], float s, uint32_t idx0, uint32_t seed)
+__device__ __forceinline__ uint32_t fast_encode_m4(const float (&x)[4], float s, float y, uint32_t idx0, uint32_t seed)
 {
     uint32_t r[4] = {0U, 0U, 0U, 0U};
     if (SR) hash4(idx0, seed, r);
     float q[4];
     if (__builtin_expect(fast_scale(s), 1)) {
-        const float y = __frcp_rn(s);
         const f2x Y = pk2(y, y), NS = pk2(-s, -s);
         up2(div2(pk2(x[0], x[1]), Y, NS), q[0], q[1]);
         up2(div2(pk2(x[2], x[3]), Y, NS), q[2], q[3]);
@@ -688,13 +687,12 @@ __device__ __forceinline__ uint32_t fast_encode_m4(const float (&x)[4], float s,
 // u = sqrt(max(v, 0)): never NaN and, with s in Markstein's range, finite, so the quotients need no NaN
 // or sign handling; s outside that range (u infinite or tiny) takes the exact out-of-line path.
 template <bool SR>
-__device__ __forceinline__ uint32_t fast_encode_u4(const float (&x)[4], float s, uint32_t idx0, uint32_t seed)
+__device__ __forceinline__ uint32_t fast_encode_u4(const float (&x)[4], float s, float y, uint32_t idx0, uint32_t seed)
 {
     uint32_t r[4] = {0U, 0U, 0U, 0U};
     if (SR) hash4(idx0, seed, r);
     float q[4];
     if (__builtin_expect(fast_scale(s), 1)) {
-        const float y = __frcp_rn(s);
         const f2x Y = pk2(y, y), NS = pk2(-s, -s);
         up2(div2(pk2(x[0], x[1]), Y, NS), q[0], q[1]);
         up2(div2(pk2(x[2], x[3]), Y, NS), q[2], q[3]);
@@ -704,10 +702,11 @@ __device__ __forceinline__ uint32_t fast_encode_u4(const float (&x)[4], float s,
     return enc4_fp8_slow<false, SR>(d.x, d.y, d.z, d.w, r[0], r[1], r[2], r[3]);
 }
 
-template <int ALGO, int PT, int GT, bool SR>
-__device__ __forceinline__ void fast_fp8(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+// Lion with an FP8 moment: per half tile, warp w owns block w (4 elements per lane).
+template <int PT, int GT, bool SR>
+__device__ __forceinline__ void fast_fp8_lion(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
 {
-    using C = Cfg<ALGO, ABX_DT_FP8, PT, GT>;
+    using C = Cfg<ABX_ALGO_LION, ABX_DT_FP8, PT, GT>;
     const Coef c = S.c;
     const Coef2 c2 = coef2(c);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -726,49 +725,93 @@ __device__ __forceinline__ void fast_fp8(const KSeg& S, int64_t base, const uint
         up2(mul2(pk2(mt[2], mt[3]), pk2(sm, sm)), mt[2], mt[3]);
         fast_grad4<GT>(st + C::OFF_G + e0 * C::GB, gs, g);
         fast_master4<PT>(st + C::OFF_P + e0 * C::PB, st + C::OFF_L + e0, p);
-        if constexpr (ALGO == ABX_ALGO_LION) {
-            lion2(p[0], p[1], g[0], g[1], mt[0], mt[1], c2, c.step);
-            lion2(p[2], p[3], g[2], g[3], mt[2], mt[3], c2, c.step);
-            store_master4<PT, SR>(S, i0, 4, p);
-            store_out4(S, i0, 4, p);
-            const float am = warp_max_nonneg(absmax4(mt));
-            const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
-            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode_m4<SR>(mt, scm, idx0, S.s_m);
-            if (lane == 0) S.m_scale[blk0 + bt] = scm;
-        } else {
-            const float* swv = reinterpret_cast<const float*>(st + C::OFF_SV + (reinterpret_cast<uintptr_t>(S.v_scale + blk0) & 15));
-            const float su = swv[bt];
-            float vt[4], ut[4];
-            dec4_fp8<false>(*reinterpret_cast<const uint32_t*>(st + C::OFF_V + e0), vt);
-            {
-                const f2x SU = pk2(su, su);
-                const f2x U01 = mul2(pk2(vt[0], vt[1]), SU), U23 = mul2(pk2(vt[2], vt[3]), SU);
-                up2(mul2(U01, U01), vt[0], vt[1]);
-                up2(mul2(U23, U23), vt[2], vt[3]);
-            }
-            if (i0 + kGroup <= S.fused_end) {
-                adamw2_fused(p[0], p[1], g[0], g[1], mt[0], mt[1], vt[0], vt[1], c2, ut[0], ut[1]);
-                adamw2_fused(p[2], p[3], g[2], g[3], mt[2], mt[3], vt[2], vt[3], c2, ut[2], ut[3]);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    p[k] = i0 + k < S.fused_end ? adamw_elem_sq<true>(p[k], g[k], mt[k], vt[k], ut[k], c)
-                                                : adamw_elem_sq<false>(p[k], g[k], mt[k], vt[k], ut[k], c);
-            }
-            store_master4<PT, SR>(S, i0, 4, p);
-            store_out4(S, i0, 4, p);
-            // u = sqrt(max(v, 0)) (csrc:1000): v >= 0 here, so only a NaN v differs, and fmaxf maps it to 0
-#pragma unroll
-            for (int k = 0; k < 4; ++k) ut[k] = fmaxf(ut[k], 0.0f);
-            const float am = warp_max_nonneg(absmax4(mt));
-            const float au = warp_max_nonneg(fmaxf(fmaxf(ut[0], ut[1]), fmaxf(ut[2], ut[3])));
-            const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
-            const float scu = au > 0.0f ? scale_of<false>(au) : 1.0f;
-            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode_m4<SR>(mt, scm, idx0, S.s_m);
-            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.v) + i0) = fast_encode_u4<SR>(ut, scu, idx0, S.s_v);
-            if (lane == 0) { S.m_scale[blk0 + bt] = scm; S.v_scale[blk0 + bt] = scu; }
-        }
+        lion2(p[0], p[1], g[0], g[1], mt[0], mt[1], c2, c.step);
+        lion2(p[2], p[3], g[2], g[3], mt[2], mt[3], c2, c.step);
+        store_master4<PT, SR>(S, i0, 4, p);
+        store_out4(S, i0, 4, p);
+        const float am = warp_max_nonneg(absmax4(mt));
+        const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
+        *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) =
+            fast_encode_m4<SR>(mt, scm, __frcp_rn(scm), idx0, S.s_m);
+        if (lane == 0) S.m_scale[blk0 + bt] = scm;
     }
+}
+
+// AdamW with FP8 moments.  Warp w owns block w of each half tile (4 elements per lane).  Both halves are
+// updated first, keeping their new m and u = sqrt(v); then the warp's four block scales (m and u of each
+// half) are computed together, lane 4j+q computing scale q -- the scalar work of four blocks in one pass --
+// and broadcast with shuffles; then the four groups of codes are encoded.
+template <int PT, int GT, bool SR>
+__device__ __forceinline__ void fast_fp8_adamw(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+{
+    using C = Cfg<ABX_ALGO_ADAMW, ABX_DT_FP8, PT, GT>;
+    const Coef c = S.c;
+    const Coef2 c2 = coef2(c);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t blk0 = base >> 7;   // first block of the tile
+    const float* swm = reinterpret_cast<const float*>(st + C::OFF_SM + (reinterpret_cast<uintptr_t>(S.m_scale + blk0) & 15));
+    const float* swv = reinterpret_cast<const float*>(st + C::OFF_SV + (reinterpret_cast<uintptr_t>(S.v_scale + blk0) & 15));
+    float mt[2][4], ut[2][4], mx[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e0 = h * kHalf + threadIdx.x * kGroup;
+        const int64_t i0 = base + e0;
+        const int bt = h * kConsumerWarps + warp;   // this warp's block within the tile
+        float g[4], p[4], vt[4];
+        const float sm = swm[bt], su = swv[bt];
+        dec4_fp8<true>(*reinterpret_cast<const uint32_t*>(st + C::OFF_M + e0), mt[h]);
+        up2(mul2(pk2(mt[h][0], mt[h][1]), pk2(sm, sm)), mt[h][0], mt[h][1]);
+        up2(mul2(pk2(mt[h][2], mt[h][3]), pk2(sm, sm)), mt[h][2], mt[h][3]);
+        dec4_fp8<false>(*reinterpret_cast<const uint32_t*>(st + C::OFF_V + e0), vt);
+        {
+            const f2x SU = pk2(su, su);
+            const f2x U01 = mul2(pk2(vt[0], vt[1]), SU), U23 = mul2(pk2(vt[2], vt[3]), SU);
+            up2(mul2(U01, U01), vt[0], vt[1]);
+            up2(mul2(U23, U23), vt[2], vt[3]);
+        }
+        fast_grad4<GT>(st + C::OFF_G + e0 * C::GB, gs, g);
+        fast_master4<PT>(st + C::OFF_P + e0 * C::PB, st + C::OFF_L + e0, p);
+        if (i0 + kGroup <= S.fused_end) {
+            adamw2_fused(p[0], p[1], g[0], g[1], mt[h][0], mt[h][1], vt[0], vt[1], c2, ut[h][0], ut[h][1]);
+            adamw2_fused(p[2], p[3], g[2], g[3], mt[h][2], mt[h][3], vt[2], vt[3], c2, ut[h][2], ut[h][3]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                p[k] = i0 + k < S.fused_end ? adamw_elem_sq<true>(p[k], g[k], mt[h][k], vt[k], ut[h][k], c)
+                                            : adamw_elem_sq<false>(p[k], g[k], mt[h][k], vt[k], ut[h][k], c);
+        }
+        store_master4<PT, SR>(S, i0, 4, p);
+        store_out4(S, i0, 4, p);
+        // u = sqrt(max(v, 0)) (csrc:1000): v >= 0 here, so only a NaN v differs, and fmaxf maps it to 0
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ut[h][k] = fmaxf(ut[h][k], 0.0f);
+        mx[2 * h] = warp_max_nonneg(absmax4(mt[h]));
+        mx[2 * h + 1] = warp_max_nonneg(fmaxf(fmaxf(ut[h][0], ut[h][1]), fmaxf(ut[h][2], ut[h][3])));
+    }
+    // lane 4j+q: scale q of (m half 0, u half 0, m half 1, u half 1); E4M3 for m, E5M2 for u
+    const int q = lane & 3;
+    const float amax = q == 0 ? mx[0] : (q == 1 ? mx[1] : (q == 2 ? mx[2] : mx[3]));
+    const bool e4 = (q & 1) == 0;
+    const float sc = amax > 0.0f ? scale_fmt(amax, e4 ? 448.0f : 57344.0f, e4 ? 0x1.24924ap-9f : 0x1.24924ap-16f)
+                                 : 1.0f;
+    const float rc = __frcp_rn(sc);
+    if (lane < 4) ((q & 1) ? S.v_scale : S.m_scale)[blk0 + (q >> 1) * kConsumerWarps + warp] = sc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int64_t i0 = base + h * kHalf + threadIdx.x * kGroup;
+        const uint32_t idx0 = S.off32 + (uint32_t)i0;
+        const float scm = __shfl_sync(0xffffffffU, sc, 2 * h), ym = __shfl_sync(0xffffffffU, rc, 2 * h);
+        const float scu = __shfl_sync(0xffffffffU, sc, 2 * h + 1), yu = __shfl_sync(0xffffffffU, rc, 2 * h + 1);
+        *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode_m4<SR>(mt[h], scm, ym, idx0, S.s_m);
+        *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.v) + i0) = fast_encode_u4<SR>(ut[h], scu, yu, idx0, S.s_v);
+    }
+}
+
+template <int ALGO, int PT, int GT, bool SR>
+__device__ __forceinline__ void fast_fp8(const KSeg& S, int64_t base, const uint8_t* st, const float* gs)
+{
+    if constexpr (ALGO == ABX_ALGO_LION) fast_fp8_lion<PT, GT, SR>(S, base, st, gs);
+    else fast_fp8_adamw<PT, GT, SR>(S, base, st, gs);
 }
 
 template <int ALGO, int MV, int PT, int GT, bool SR>
