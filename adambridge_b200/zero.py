@@ -214,6 +214,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._segs = self._build_segments()
         self.trace: list | None = None   # (start, end) CUDA events of every update launch, when a list
         self.norm_trace: list = []       # (start, end) events of the norm kernels, while ``trace`` is a list
+        self.release_grads = True
+        self._hooked = False
+        self._hook_handles: list = []
         self._clip_coef: torch.Tensor | None = None
         self._norm_state = None
 
@@ -320,17 +323,113 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     @torch.no_grad()
     def step(self, closure=None):
         """Reduce-scatter (mean) the local gradients, update this rank's shard, all-gather the weights.
-        After :meth:`clip_grad_norm_` the gradients are already reduced and the update applies the clip."""
+        After :meth:`clip_grad_norm_` the gradients are already reduced and the update applies the clip;
+        with :meth:`attach_hooks` the reduce-scatters ran during backward."""
         loss = None
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        if self._hooked:
+            self._finish_hooked_reduce()
         if self._clip_coef is not None:
             coef, self._clip_coef = self._clip_coef, None
             self._run(None, g_scale=coef, synced=True)
+        elif self._hooked:
+            self._run(None)
         else:
             self._run(self._local_grads())
+        self._reset_hook_state()
         return loss
+
+    # ------------------------------------------------------------------ gradients reduced during backward
+
+    def attach_hooks(self, model: torch.nn.Module | None = None) -> "ZeroAdamBridge":
+        """Reduce-scatter the gradients during backward (the data-parallel gradient path).
+
+        A post-accumulate-grad hook copies each parameter's finished gradient into the flat gradient buffer
+        (and, with ``release_grads``, frees ``p.grad``); when every parameter overlapping a round of the flat
+        layout has arrived, that round's reduce-scatter (mean) starts on the comm stream, so it overlaps the
+        rest of backward -- backward runs roughly in reverse parameter order, so the last rounds go first.
+        ``step()`` then waits for the reduce-scatters and updates.  The overlap is per round: construct the
+        optimizer with ``rounds`` > 1 for it.  Every parameter must receive exactly one gradient per step."""
+        if self._hooked:
+            return self
+        wanted = None if model is None else {id(p) for p in model.parameters()}
+        L = self.layout
+        self._rounds_of = []
+        for i in range(len(self._params)):
+            a, b = L.flat_slice(i)
+            span = L.world * L.chunk
+            self._rounds_of.append(list(range(a // span, (max(b, a + 1) - 1) // span + 1)))
+        hook = torch.compiler.disable(self._on_grad_ready)
+        self._index_of = {id(p): i for i, p in enumerate(self._params)}
+        for p in self._params:
+            if p.requires_grad and (wanted is None or id(p) in wanted):
+                self._hook_handles.append(p.register_post_accumulate_grad_hook(hook))
+        self._hooked = True
+        self._reset_hook_state()
+        return self
+
+    def detach_hooks(self) -> None:
+        for h in self._hook_handles:
+            h.remove()
+        self._hook_handles.clear()
+        self._hooked = False
+
+    def _reset_hook_state(self) -> None:
+        if not self._hooked:
+            return
+        L = self.layout
+        self._pending = [0] * L.rounds
+        for rounds in self._rounds_of:
+            for r in rounds:
+                self._pending[r] += 1
+        self._arrived = [False] * len(self._params)
+        self._reduced = [False] * L.rounds
+
+    def _on_grad_ready(self, p: torch.Tensor) -> None:
+        i = self._index_of[id(p)]
+        if self._arrived[i]:
+            raise RuntimeError("ZeroAdamBridge: parameter received a second gradient before step()")
+        self._arrived[i] = True
+        a, b = self.layout.flat_slice(i)
+        with torch.no_grad():
+            self._flat_grad_buffer()[a:b].copy_(p.grad.reshape(-1))
+        if self.release_grads:
+            p.grad = None
+        for r in self._rounds_of[i]:
+            self._pending[r] -= 1
+            if self._pending[r] == 0:
+                self._reduce_round(r)
+
+    def _reduce_round(self, r: int) -> None:
+        """Reduce-scatter round ``r`` of the flat gradients into this rank's shard (comm stream, ordered after
+        the work the current stream has enqueued so far)."""
+        L = self.layout
+        flat = self._flat_grad_buffer()
+        shard = self.grad_shard[r * L.chunk:(r + 1) * L.chunk]
+        src = flat[slice(*L.round_range(r))]
+        cur = torch.cuda.current_stream(self.device)
+        with torch.no_grad(), torch.cuda.device(self.device):
+            if self._comm_stream is None:
+                self._update_stream.wait_stream(cur)
+                with torch.cuda.stream(self._update_stream):
+                    shard.copy_(src)
+            else:
+                self._comm_stream.wait_stream(cur)
+                with torch.cuda.stream(self._comm_stream):
+                    dist.reduce_scatter_tensor(shard, src, op=dist.ReduceOp.AVG, group=self.pg)
+        self._reduced[r] = True
+
+    def _finish_hooked_reduce(self) -> None:
+        """Before the update of a hooked step: every parameter's gradient arrived; the update stream waits for
+        the reduce-scatters."""
+        missing = [i for i, done in enumerate(self._arrived) if not done]
+        if missing:
+            raise RuntimeError(f"parameters {missing[:8]} have no gradient this step: ZeRO steps update every "
+                               "parameter (with hooks attached, each needs exactly one gradient per step)")
+        if self._comm_stream is not None:
+            self._update_stream.wait_stream(self._comm_stream)
 
     @torch.no_grad()
     def step_shard(self, grad_shard: torch.Tensor | None = None) -> None:
@@ -378,9 +477,13 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         with every gradient scaled by the coefficient inside the update kernel."""
         if float(norm_type) != 2.0:
             raise ValueError("clip_grad_norm_ computes the L2 norm (norm_type=2) only")
+        cur = torch.cuda.current_stream(self.device)
+        if self._hooked:   # reduced during backward
+            self._finish_hooked_reduce()
+            self._update_stream.wait_stream(cur)
+            return self._clip_shard(max_norm, cur)
         flat = self._local_grads()
         L = self.layout
-        cur = torch.cuda.current_stream(self.device)
         upd, comm = self._update_stream, self._comm_stream
         upd.wait_stream(cur)
         with torch.cuda.device(self.device):

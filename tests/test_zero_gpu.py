@@ -265,3 +265,91 @@ def test_zero_two_gpus_checkpoint_gather_and_resume(tmp_path, gather):
         for g, w in zip(got, pa):
             assert torch.equal(g, w.detach().cpu())
     oa.close()
+
+
+# ---------------------------------------------------------------------------------- gradients reduced in backward
+
+class _Mlp(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.layers = torch.nn.ModuleList(torch.nn.Linear(96, 96) for _ in range(4))
+        self.head = torch.nn.Linear(96, 7)
+
+    def forward(self, x):
+        for layer in self.layers:
+            x = torch.nn.functional.gelu(layer(x))
+        return self.head(x)
+
+
+def _mlp_pair(device):
+    torch.manual_seed(0)
+    a = _Mlp().to(device, torch.bfloat16)
+    b = _Mlp().to(device, torch.bfloat16)
+    b.load_state_dict(a.state_dict())
+    return a, b
+
+
+def _mlp_loss(model, step, rank, device):
+    g = torch.Generator(device=device).manual_seed(100 * step + rank)
+    x = torch.randn(32, 96, device=device, generator=g).to(torch.bfloat16)
+    return model(x).float().square().mean()
+
+
+def _hooks_vs_step(rank, world, device, gather, clip, steps=3):
+    """The same model trained by a hooked and by a step-mode ZeRO optimizer: identical weights."""
+    ma, mb = _mlp_pair(device)
+    kw = dict(lr=2e-3, precision="bf16", seed=3, rounds=3)
+    if gather is not None:
+        kw["gather"] = gather
+    oa = ZeroAdamBridge(list(ma.parameters()), **kw).attach_hooks(ma)
+    ob = ZeroAdamBridge(list(mb.parameters()), **kw)
+    for step in range(1, steps + 1):
+        for model, opt in ((ma, oa), (mb, ob)):
+            _mlp_loss(model, step, rank, device).backward()
+            if clip is not None:
+                opt.clip_grad_norm_(clip)
+            opt.step()
+            opt.zero_grad()
+    torch.cuda.synchronize()
+    return [p.detach().cpu() for p in ma.parameters()], [p.detach().cpu() for p in mb.parameters()]
+
+
+@pytest.mark.parametrize("clip", [None, 0.05])
+def test_zero_hooks_equal_step_world1(clip):
+    got, want = _hooks_vs_step(0, 1, "cuda", None, clip)
+    assert all(torch.equal(a, b) for a, b in zip(got, want))
+
+
+def test_zero_hooks_reject_a_second_gradient():
+    ma, _ = _mlp_pair("cuda")
+    opt = ZeroAdamBridge(list(ma.parameters()), lr=1e-3, precision="bf16", rounds=2).attach_hooks(ma)
+    _mlp_loss(ma, 1, 0, "cuda").backward()
+    with pytest.raises(RuntimeError, match="second gradient"):
+        _mlp_loss(ma, 2, 0, "cuda").backward()
+
+
+def _hooks_rank(rank, world, port, out_dir, gather, clip):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        got, want = _hooks_vs_step(rank, world, f"cuda:{rank}", gather, clip)
+        with open(os.path.join(out_dir, f"hooks{rank}.pkl"), "wb") as f:
+            pickle.dump((got, want), f)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("gather,clip", [("nccl", None), ("p2p", None), ("p2p", 0.05)])
+def test_zero_two_gpus_hooks_equal_step(tmp_path, gather, clip):
+    """Reduce-scatters issued from the backward hooks, round by round, give the weights of step()'s
+    reduce-scatters on every rank (ranks see different data, so the average matters)."""
+    mp.start_processes(_hooks_rank, args=(2, _free_port(), str(tmp_path), gather, clip), nprocs=2,
+                       start_method="spawn", join=True)
+    ranks = [pickle.load(open(tmp_path / f"hooks{r}.pkl", "rb")) for r in range(2)]
+    for got, want in ranks:
+        assert all(torch.equal(a, b) for a, b in zip(got, want))
+    assert all(torch.equal(a, b) for a, b in zip(ranks[0][0], ranks[1][0]))   # replicas agree
