@@ -51,7 +51,8 @@ constexpr int kGroup = 4;                              // elements per thread pe
 constexpr int kHalf = kConsumerWarps * 32 * kGroup;    // 1024
 constexpr int kTile = 2 * kHalf;                       // 2048 elements per tile
 constexpr int kMaxSegs = 64;                           // segments per launch (parameter block ~10 KB)
-constexpr int kSmemTarget = 72 * 1024;                 // ring bytes per CTA (about three CTAs per SM)
+constexpr int kMinCtasPerSm = 4;                       // residency the register budget is set for (<= 56 regs)
+constexpr int kSmemTarget = 52 * 1024;                 // ring bytes per CTA (four CTAs per SM)
 constexpr uint32_t kSpinLimit = 1u << 22;              // mbarrier polls before a wait gives up
 constexpr int kMaxReplicas = 7;                        // out replicas per segment (peers of an 8-GPU node)
 
@@ -835,7 +836,7 @@ __device__ __forceinline__ const void* window_start(const void* p)
 }
 
 template <int ALGO, int MV, int PT, int GT, int NSEG>
-__global__ void __launch_bounds__(kThreads, 3) update_kernel(const __grid_constant__ KArgs<NSEG> a)
+__global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const __grid_constant__ KArgs<NSEG> a)
 {
     using C = Cfg<ALGO, MV, PT, GT>;
     extern __shared__ __align__(128) uint8_t smem[];
