@@ -556,6 +556,85 @@ __host__ __device__ constexpr int ring_offset(int stages)
 __device__ __forceinline__ bool staged_tile(const KSeg& S, int64_t base) { return S.tma_ok && base + kTile <= S.n; }
 
 // ---- fast path: a whole tile staged in shared memory ------------------------------------
+
+// Fast-path stores.  In a staged tile every store address is aligned for its vector (the segment
+// passed the bulk-copy alignment check, which includes the 4-element alignment of out, and peers'
+// copies of out sit at the same offsets of identically aligned buffers).  They are st.global
+// statements: the compiler then knows that they cannot write the shared-memory tile header, so it
+// keeps the header's fields in registers instead of reloading them after every store.  The fence at
+// the kernel's end is an asm statement too, so it stays after them.
+__device__ __forceinline__ size_t gaddr(const void* p) { return __cvta_generic_to_global(p); }
+
+__device__ __forceinline__ void stg_f32x4(void* p, float a, float b, float c, float d)
+{
+    asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gaddr(p)), "f"(a), "f"(b), "f"(c), "f"(d));
+}
+
+__device__ __forceinline__ void stg_b32x2(void* p, uint32_t a, uint32_t b)
+{
+    asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(gaddr(p)), "r"(a), "r"(b));
+}
+
+__device__ __forceinline__ void stg_b32(void* p, uint32_t a)
+{
+    asm volatile("st.global.b32 [%0], %1;" ::"l"(gaddr(p)), "r"(a));
+}
+
+template <int PT, bool SR>
+__device__ __forceinline__ void fast_store_master4(const KSeg& S, int64_t i0, float (&p)[4])
+{
+    if constexpr (PT == ABX_DT_F24) {
+        uint32_t b[4], r[4] = {0U, 0U, 0U, 0U};
+        if (SR) hash4(S.off32 + (uint32_t)i0, S.s_p, r);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            b[k] = f24_bits(f2u(p[k]), SR, r[k]);
+            p[k] = u2f(b[k]);
+        }
+        const uint32_t lo = __byte_perm(__byte_perm(b[0], b[1], 0x0051), __byte_perm(b[2], b[3], 0x0051), 0x5410);
+        stg_b32x2(static_cast<uint16_t*>(S.p) + i0, pack_hi16(b[0], b[1]), pack_hi16(b[2], b[3]));
+        stg_b32(S.p_lo + i0, lo);
+    } else {
+        stg_f32x4(static_cast<float*>(S.p) + i0, p[0], p[1], p[2], p[3]);
+    }
+}
+
+__device__ __forceinline__ void fast_store_out4(const KSeg& S, int64_t i0, const float (&p)[4])
+{
+    if (S.out_dt == ABX_DT_BF16) {
+        const uint32_t w0 = pack_bf16_rne(p[0], p[1]), w1 = pack_bf16_rne(p[2], p[3]);
+        char* o = reinterpret_cast<char*>(static_cast<uint16_t*>(S.out) + i0);
+        stg_b32x2(o, w0, w1);
+        for (int j = 0; j < S.nrep; ++j) stg_b32x2(o + S.rep_delta[j], w0, w1);
+    } else if (S.out_dt == ABX_DT_F32) {
+        char* o = reinterpret_cast<char*>(static_cast<float*>(S.out) + i0);
+        stg_f32x4(o, p[0], p[1], p[2], p[3]);
+        for (int j = 0; j < S.nrep; ++j) stg_f32x4(o + S.rep_delta[j], p[0], p[1], p[2], p[3]);
+    }
+}
+
+template <int MV, bool SR>
+__device__ __forceinline__ void fast_store_moment4(void* base, int64_t i0, const float (&x)[4], uint32_t seed,
+                                                   uint32_t idx0)
+{
+    if constexpr (MV == ABX_DT_BF16) {
+        uint32_t w0, w1;
+        if constexpr (SR) {
+            uint32_t b[4], r[4];
+            hash4(idx0, seed, r);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) b[k] = f2u(x[k]) + (r[k] & 0xffffU);
+            w0 = pack_hi16(b[0], b[1]);
+            w1 = pack_hi16(b[2], b[3]);
+        } else {
+            w0 = pack_bf16_rne(x[0], x[1]);
+            w1 = pack_bf16_rne(x[2], x[3]);
+        }
+        stg_b32x2(static_cast<uint16_t*>(base) + i0, w0, w1);
+    } else {
+        stg_f32x4(static_cast<float*>(base) + i0, x[0], x[1], x[2], x[3]);
+    }
+}
 // Every element is valid and every buffer aligned, so loads come from shared memory and stores go
 // straight to HBM as vectors, with no per-element masks or alignment branches.
 
@@ -627,8 +706,8 @@ __device__ __forceinline__ void fast_dense(const KSeg& S, int64_t base, const ui
         if constexpr (ALGO == ABX_ALGO_LION) {
             lion2(p[0], p[1], g[0], g[1], m[0], m[1], c2, c.step);
             lion2(p[2], p[3], g[2], g[3], m[2], m[3], c2, c.step);
-            store_master4<PT, SR>(S, i0, 4, p);
-            store_moment4<MV, SR>(S.m, i0, 4, true, m, S.s_m, idx0);
+            fast_store_master4<PT, SR>(S, i0, p);
+            fast_store_moment4<MV, SR>(S.m, i0, m, S.s_m, idx0);
         } else {
             float v[4];
             fast_moment4<MV>(st + C::OFF_V + e0 * C::MB, v);
@@ -640,11 +719,11 @@ __device__ __forceinline__ void fast_dense(const KSeg& S, int64_t base, const ui
 #pragma unroll
                 for (int k = 0; k < 4; ++k) p[k] = adamw_elem_sel(p[k], g[k], m[k], v[k], c, i0 + k < S.fused_end);
             }
-            store_master4<PT, SR>(S, i0, 4, p);
-            store_moment4<MV, SR>(S.m, i0, 4, true, m, S.s_m, idx0);
-            store_moment4<MV, SR>(S.v, i0, 4, true, v, S.s_v, idx0);
+            fast_store_master4<PT, SR>(S, i0, p);
+            fast_store_moment4<MV, SR>(S.m, i0, m, S.s_m, idx0);
+            fast_store_moment4<MV, SR>(S.v, i0, v, S.s_v, idx0);
         }
-        store_out4(S, i0, 4, p);
+        fast_store_out4(S, i0, p);
     }
 }
 
@@ -728,13 +807,12 @@ __device__ __forceinline__ void fast_fp8_lion(const KSeg& S, int64_t base, const
         fast_master4<PT>(st + C::OFF_P + e0 * C::PB, st + C::OFF_L + e0, p);
         lion2(p[0], p[1], g[0], g[1], mt[0], mt[1], c2, c.step);
         lion2(p[2], p[3], g[2], g[3], mt[2], mt[3], c2, c.step);
-        store_master4<PT, SR>(S, i0, 4, p);
-        store_out4(S, i0, 4, p);
+        fast_store_master4<PT, SR>(S, i0, p);
+        fast_store_out4(S, i0, p);
         const float am = warp_max_nonneg(absmax4(mt));
         const float scm = am > 0.0f ? scale_of<true>(am) : 1.0f;
-        *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) =
-            fast_encode_m4<SR>(mt, scm, __frcp_rn(scm), idx0, S.s_m);
-        if (lane == 0) S.m_scale[blk0 + bt] = scm;
+        stg_b32(static_cast<uint8_t*>(S.m) + i0, fast_encode_m4<SR>(mt, scm, __frcp_rn(scm), idx0, S.s_m));
+        if (lane == 0) stg_b32(S.m_scale + blk0 + bt, f2u(scm));
     }
 }
 
@@ -781,8 +859,8 @@ __device__ __forceinline__ void fast_fp8_adamw(const KSeg& S, int64_t base, cons
                 p[k] = i0 + k < S.fused_end ? adamw_elem_sq<true>(p[k], g[k], mt[h][k], vt[k], ut[h][k], c)
                                             : adamw_elem_sq<false>(p[k], g[k], mt[h][k], vt[k], ut[h][k], c);
         }
-        store_master4<PT, SR>(S, i0, 4, p);
-        store_out4(S, i0, 4, p);
+        fast_store_master4<PT, SR>(S, i0, p);
+        fast_store_out4(S, i0, p);
         // u = sqrt(max(v, 0)) (csrc:1000): v >= 0 here, so only a NaN v differs, and fmaxf maps it to 0
 #pragma unroll
         for (int k = 0; k < 4; ++k) ut[h][k] = fmaxf(ut[h][k], 0.0f);
@@ -796,15 +874,15 @@ __device__ __forceinline__ void fast_fp8_adamw(const KSeg& S, int64_t base, cons
     const float sc = amax > 0.0f ? scale_fmt(amax, e4 ? 448.0f : 57344.0f, e4 ? 0x1.24924ap-9f : 0x1.24924ap-16f)
                                  : 1.0f;
     const float rc = __frcp_rn(sc);
-    if (lane < 4) ((q & 1) ? S.v_scale : S.m_scale)[blk0 + (q >> 1) * kConsumerWarps + warp] = sc;
+    if (lane < 4) stg_b32(((q & 1) ? S.v_scale : S.m_scale) + blk0 + (q >> 1) * kConsumerWarps + warp, f2u(sc));
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const int64_t i0 = base + h * kHalf + threadIdx.x * kGroup;
         const uint32_t idx0 = S.off32 + (uint32_t)i0;
         const float scm = __shfl_sync(0xffffffffU, sc, 2 * h), ym = __shfl_sync(0xffffffffU, rc, 2 * h);
         const float scu = __shfl_sync(0xffffffffU, sc, 2 * h + 1), yu = __shfl_sync(0xffffffffU, rc, 2 * h + 1);
-        *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.m) + i0) = fast_encode_m4<SR>(mt[h], scm, ym, idx0, S.s_m);
-        *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(S.v) + i0) = fast_encode_u4<SR>(ut[h], scu, yu, idx0, S.s_v);
+        stg_b32(static_cast<uint8_t*>(S.m) + i0, fast_encode_m4<SR>(mt[h], scm, ym, idx0, S.s_m));
+        stg_b32(static_cast<uint8_t*>(S.v) + i0, fast_encode_u4<SR>(ut[h], scu, yu, idx0, S.s_v));
     }
 }
 
@@ -920,8 +998,9 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
         if (lane == 0) mbar_arrive(&empty[s]);
     }
     // Stores into peers' memory (replicated out) are performed system-wide before this CTA ends, so the
-    // kernel's completion -- and any barrier the caller takes after it -- covers them.
-    __threadfence_system();
+    // kernel's completion -- and any barrier the caller takes after it -- covers them.  (The fast path's
+    // stores are asm statements; so is this fence, which keeps it after them.)
+    asm volatile("fence.sc.sys;" ::: "memory");
 }
 
 // ---- host side ---------------------------------------------------------------------------
