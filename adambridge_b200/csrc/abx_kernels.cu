@@ -937,10 +937,10 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
     if (warp == kConsumerWarps) {
         // ---- producer: one lane describes each tile and streams staged ones into the ring ----
         if (lane != 0) return;
-        int k = 0;
+        int k = 0, s = 0;
+        uint32_t ph = 0;   // parity of the current pass over the ring (s and ph track k % S and (k / S) & 1)
         for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
-            const int s = k % S;
-            if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
+            if (!mbar_wait(&empty[s], ph ^ 1)) break;
             const int si = find_segment(a, t);
             const KSeg& Sg = a.seg[si];
             const int64_t base = (t - Sg.tile_begin) * kTile;
@@ -972,6 +972,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
             } else {
                 mbar_arrive(&full[s]);   // consumers read this tile from global memory
             }
+            if (++s == S) { s = 0; ph ^= 1; }
         }
         // never leave with bulk copies in flight into this CTA's shared memory
         for (int j = k - S < 0 ? 0 : k - S; j < k; ++j) mbar_wait(&full[j % S], (j / S) & 1);
@@ -980,10 +981,10 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
 
     // ---- consumers ----
     const float* gs = a.g_scale;
-    int k = 0;
-    for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
-        const int s = k % S;
-        if (!mbar_wait(&full[s], (k / S) & 1)) return;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x) {
+        if (!mbar_wait(&full[s], ph)) return;
         const TileMeta tm = hdr[s].meta;
         const KSeg& Sg = hdr[s].seg;
         if (tm.staged) {
@@ -996,6 +997,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == S) { s = 0; ph ^= 1; }
     }
     // Stores into peers' memory (replicated out) are performed system-wide before this CTA ends, so the
     // kernel's completion -- and any barrier the caller takes after it -- covers them.  (The fast path's
