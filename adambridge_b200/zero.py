@@ -215,6 +215,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self.trace: list | None = None   # (start, end) CUDA events of every update launch, when a list
         self.norm_trace: list = []       # (start, end) events of the norm kernels, while ``trace`` is a list
         self.release_grads = True
+        self._copy_streams: tuple | None = None
         self._hooked = False
         self._hook_handles: list = []
         self._clip_coef: torch.Tensor | None = None
@@ -432,15 +433,30 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             self._update_stream.wait_stream(self._comm_stream)
 
     @torch.no_grad()
-    def step_shard(self, grad_shard: torch.Tensor | None = None) -> None:
-        """Update from this rank's reduced gradient shard (default: ``self.grad_shard``) and all-gather."""
-        if grad_shard is not None and grad_shard.data_ptr() != self.grad_shard.data_ptr():
+    def step_shard(self, grad_shard: torch.Tensor | None = None, weights_out: torch.Tensor | None = None) -> None:
+        """Update from this rank's reduced gradient shard (default: ``self.grad_shard``) and all-gather.
+
+        ``grad_shard`` may be a pinned host tensor (``shard_numel`` gradients, round-major): it is copied in
+        round by round on a copy stream, each round's copy overlapping the update of the round before.
+        ``weights_out``, a pinned host tensor of ``shard_numel`` weights, receives this rank's updated weight
+        shard round by round, each copy overlapping the next round's update.  Together they run the step as
+        a host pipeline with both PCIe directions busy at once; the overlap is per round (``rounds`` > 1)."""
+        L = self.layout
+        host_in = grad_shard if grad_shard is not None and not grad_shard.is_cuda else None
+        if host_in is not None and (host_in.numel() != L.shard_numel or host_in.dtype != self.grad_dtype):
+            raise ValueError(f"a host gradient shard must hold {L.shard_numel} {self.grad_dtype} elements")
+        if weights_out is not None and (weights_out.is_cuda or weights_out.numel() != L.shard_numel
+                                        or weights_out.dtype != self.dtype):
+            raise ValueError(f"weights_out must be a host tensor of {L.shard_numel} {self.dtype} elements")
+        if grad_shard is not None and host_in is None and grad_shard.data_ptr() != self.grad_shard.data_ptr():
             self.grad_shard.copy_(grad_shard)
         if self._clip_coef is not None:
+            if host_in is not None:
+                raise ValueError("clip_shard_grad_norm_ needs the gradient shard on the device before the step")
             coef, self._clip_coef = self._clip_coef, None
-            self._run(None, g_scale=coef, synced=True)
+            self._run(None, g_scale=coef, synced=True, host_out=weights_out)
         else:
-            self._run(None)
+            self._run(None, host_in=host_in, host_out=weights_out)
 
     # ------------------------------------------------------------------ clipping
 
@@ -535,7 +551,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         return total_coef[0].to(self.grad_dtype)
 
     def _run(self, flat_grads: torch.Tensor | None, g_scale: torch.Tensor | None = None,
-             synced: bool = False) -> None:
+             synced: bool = False, host_in: torch.Tensor | None = None, host_out: torch.Tensor | None = None) -> None:
         L = self.layout
         self._refresh()
         cur = torch.cuda.current_stream(self.device)
@@ -544,10 +560,22 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         upd.wait_stream(cur)
         if comm is not None:
             comm.wait_stream(cur)
+        h2d = d2h = None
+        if host_in is not None or host_out is not None:
+            if self._copy_streams is None:
+                self._copy_streams = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+            h2d, d2h = self._copy_streams
+            h2d.wait_stream(cur)
+            d2h.wait_stream(cur)
         with torch.cuda.device(self.device):
             if p2p and flat_grads is None and not synced:
                 self._barrier(upd)   # no peer still reads the weights this update overwrites
             for r in range(L.rounds):
+                if host_in is not None:
+                    with torch.cuda.stream(h2d):
+                        self.grad_shard[r * L.chunk:(r + 1) * L.chunk].copy_(
+                            host_in[r * L.chunk:(r + 1) * L.chunk], non_blocking=True)
+                    upd.wait_stream(h2d)
                 if flat_grads is not None:
                     shard = self.grad_shard[r * L.chunk:(r + 1) * L.chunk]
                     src = flat_grads[slice(*L.round_range(r))]
@@ -570,6 +598,11 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 if end is not None:
                     end.record(upd)
                     self.trace.append((start, end))
+                if host_out is not None:
+                    d2h.wait_stream(upd)
+                    with torch.cuda.stream(d2h):
+                        host_out[r * L.chunk:(r + 1) * L.chunk].copy_(
+                            self.flat_weights[slice(*L.rank_range(r, self.rank))], non_blocking=True)
                 if comm is not None and not p2p:
                     comm.wait_stream(upd)
                     with torch.cuda.stream(comm):
@@ -581,6 +614,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         cur.wait_stream(upd)
         if comm is not None:
             cur.wait_stream(comm)
+        if h2d is not None:
+            cur.wait_stream(h2d)
+            cur.wait_stream(d2h)
 
     # ------------------------------------------------------------------ inspection
 

@@ -266,16 +266,15 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         e2e_steps = max(1, min(args.steps, args.e2e_steps))
         host_g = torch.empty(L.shard_numel, dtype=opt.grad_dtype, pin_memory=True)
         host_g.copy_(opt.grad_shard.cpu())
-        mine = [opt.flat_weights[slice(*L.rank_range(r, rank))] for r in range(L.rounds)]
         host_w = torch.empty(L.shard_numel, dtype=opt.dtype, pin_memory=True)
 
         def e2e_step():
-            opt.grad_shard.copy_(host_g, non_blocking=True)
             if args.clip is not None:
+                opt.grad_shard.copy_(host_g, non_blocking=True)
                 opt.clip_shard_grad_norm_(args.clip)
-            opt.step_shard()
-            for r, w in enumerate(mine):
-                host_w[r * L.chunk:(r + 1) * L.chunk].copy_(w, non_blocking=True)
+                opt.step_shard(weights_out=host_w)
+            else:
+                opt.step_shard(host_g, weights_out=host_w)   # copies in and out overlap the rounds' updates
 
         e2e_step()
         torch.cuda.synchronize()
@@ -294,8 +293,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         e2e = {"value": round(n_params / (e_ms / 1e3) / 1e9, 4), "unit": "Gparams/s",
                "h2d_bytes_per_step": host_g.numel() * host_g.element_size(),
                "d2h_bytes_per_step": host_w.numel() * host_w.element_size(), "ms_per_step": round(e_ms, 3),
-               "path": "ZeroAdamBridge.step_shard with the gradient shard copied in from pinned host memory and the "
-                       "updated weight shard copied out to pinned host memory every step"}
+               "path": "ZeroAdamBridge.step_shard(host gradient shard, weights_out=host weight shard): every step "
+                       "copies the gradient shard in from pinned host memory and the updated weight shard out, "
+                       f"round by round ({L.rounds} rounds) overlapping the updates"}
         del host_g, host_w
 
     if rank != 0:
@@ -372,7 +372,8 @@ def main() -> int:
     ap.add_argument("--impl", default="abx", choices=["abx", "reference"])
     ap.add_argument("--algorithm", default="adamw", choices=["adamw", "lion"])
     ap.add_argument("--precision", default="bf16", choices=["fp32", "bf16", "fp8"])
-    ap.add_argument("--rounds", type=int, default=None)
+    ap.add_argument("--rounds", type=int, default=8,
+                    help="rounds of the ZeRO layout: the end-to-end step's host copies overlap round by round")
     ap.add_argument("--max-ctas", type=int, default=0, help="cap the update kernel's CTAs (0: every SM)")
     ap.add_argument("--gather", default="auto", choices=["auto", "p2p", "nccl"],
                     help="N > 1: all-gather fused into the update as peer stores (p2p), or NCCL's")

@@ -353,3 +353,25 @@ def test_zero_two_gpus_hooks_equal_step(tmp_path, gather, clip):
     for got, want in ranks:
         assert all(torch.equal(a, b) for a, b in zip(got, want))
     assert all(torch.equal(a, b) for a, b in zip(ranks[0][0], ranks[1][0]))   # replicas agree
+
+
+def test_zero_host_streamed_step_equals_device_step():
+    """step_shard(pinned host gradient shard, weights_out=pinned host buffer) -- copies overlapping the rounds'
+    updates -- gives the device path's weights, and weights_out holds this rank's updated weight shard."""
+    pa, pb = _params("cuda"), _params("cuda")
+    oa = ZeroAdamBridge(pa, lr=1e-3, precision="fp8", seed=3, rounds=3)
+    ob = ZeroAdamBridge(pb, lr=1e-3, precision="fp8", seed=3, rounds=3)
+    L = ob.layout
+    out = torch.empty(L.shard_numel, dtype=torch.bfloat16, pin_memory=True)
+    gen = torch.Generator().manual_seed(9)
+    for _ in range(3):
+        g = (torch.randn(L.shard_numel, generator=gen) * 1e-3).to(torch.bfloat16).pin_memory()
+        oa.step_shard(g.cuda())
+        ob.step_shard(g, weights_out=out)
+    torch.cuda.synchronize()
+    for a, b in zip(pa, pb):
+        assert torch.equal(a, b)
+    mine = torch.cat([ob.flat_weights[slice(*L.rank_range(r, 0))] for r in range(L.rounds)]).cpu()
+    assert torch.equal(out, mine)
+    with pytest.raises(ValueError):
+        ob.step_shard(g[:-1])
