@@ -36,8 +36,8 @@ BYTES_PER_PARAM = {("adamw", "bf16"): 20, ("adamw", "fp32"): 28, ("adamw", "fp8"
 # NVLink 5 peer copy measured on this pool's B200s, per direction per GPU (900 GB/s nominal): the denominator for a
 # kernel bound by its stores into the peers' memory
 NVLINK_PEER_GBS = 770.0
-MEASURED_DRAM_BYTES_PER_PARAM = {("adamw", "bf16"): (2.679314e9 + 2.621452e9) / 267923456,
-                                 ("adamw", "fp8"): (2.160244e9 + 2.103694e9) / 267923456}
+MEASURED_DRAM_BYTES_PER_PARAM = {("adamw", "bf16"): (2.679388e9 + 2.622009e9) / 267923456,
+                                 ("adamw", "fp8"): (2.160363e9 + 2.111521e9) / 267923456}
 
 
 def llama_shapes(hidden, layers, mlp, vocab, kv, tied=False):
@@ -83,17 +83,22 @@ class ClockSampler:
             self.mhz.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
             active = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
             self.reasons.update(name for name, bit in bits.items() if active & bit)
+            self._ready.set()
             self._stop.wait(self.period)
 
     def __enter__(self):
         import threading
         self._stop = threading.Event()
+        self._ready = threading.Event()
         self._thread = None
         try:
             import pynvml
             pynvml.nvmlInit()
             self._thread = threading.Thread(target=self._loop, daemon=True)
             self._thread.start()
+            self._ready.wait(5.0)   # the sampler is running before the timed region starts
+            self.mhz.clear()        # ... and only samples taken inside it are kept
+            self.reasons.clear()
         except Exception:  # noqa: BLE001 -- no NVML: the line reports no samples
             self._thread = None
         return self
