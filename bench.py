@@ -189,6 +189,73 @@ def reference_arm(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def reference_gpu_arm(args, rank: int) -> None:
+    """--impl reference-gpu: the reference's only GPU update, its gpu_state_budget path
+    (adambridge/optimizer.py:364-430, _step_gpu), on the same 7B parameter set: FP32 master weights and
+    moments on the GPU, each bf16 gradient converted with grad.to(float32), torch.optim.AdamW(fused=True),
+    then torch._foreach_copy_ of the masters into the bf16 weights.  Rank 0 only; for context beside the
+    reference's CPU arm, not part of the driver's contract."""
+    if rank != 0:
+        return
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dims = dict(LLAMA7B)
+    if args.layers is not None:
+        dims["layers"] = args.layers
+    if args.vocab is not None:
+        dims["vocab"] = args.vocab
+    shapes = llama_shapes(**dims)
+    n_params = sum(numel(sh) for sh in shapes)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    weights, masters, grads = [], [], []
+    with torch.no_grad():
+        for sh in shapes:
+            w = torch.empty(sh, dtype=torch.bfloat16, device=dev).normal_(0.0, 0.02, generator=gen)
+            weights.append(w)
+            masters.append(torch.nn.Parameter(w.float()))
+            grads.append(torch.empty(sh, dtype=torch.bfloat16, device=dev).normal_(0.0, 1e-3, generator=gen))
+    inner = torch.optim.AdamW(masters, lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, fused=True)
+
+    def step():
+        for mp, g in zip(masters, grads):
+            mp.grad = g.to(torch.float32)
+        inner.step()
+        torch._foreach_copy_(weights, masters)
+        for mp in masters:
+            mp.grad = None
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        t0.record(cur)
+        for _ in range(args.steps):
+            step()
+        t1.record(cur)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    # bytes the path moves: grad bf16 read + fp32 write, fused AdamW (p, g, m, v read; p, m, v written, fp32),
+    # master read + bf16 weight write
+    bpp = 2 + 4 + 7 * 4 + 4 + 2
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = bpp * n_params / (ms / 1e3) / 1e9
+    line = {"impl": "reference-gpu", "metric": "fused step Gparams/s (7B, the reference's GPU update)",
+            "value": round(n_params / (ms / 1e3) / 1e9, 4), "unit": "Gparams/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "llama7b-adamw-fp32-state-torch-fused (gpu_state_budget path)",
+                       "params": n_params, "tensors": len(shapes)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "basis": f"{bpp} B/param moved by grad.to(fp32) + fused AdamW + _foreach_copy_"},
+            "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 
 def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
@@ -374,7 +441,7 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="abx", choices=["abx", "reference"])
+    ap.add_argument("--impl", default="abx", choices=["abx", "reference", "reference-gpu"])
     ap.add_argument("--algorithm", default="adamw", choices=["adamw", "lion"])
     ap.add_argument("--precision", default="bf16", choices=["fp32", "bf16", "fp8"])
     ap.add_argument("--rounds", type=int, default=8,
@@ -399,6 +466,9 @@ def main() -> int:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return 0
+    if args.impl == "reference-gpu":
+        reference_gpu_arm(args, rank)
         return 0
     import datetime
 
