@@ -256,6 +256,141 @@ def reference_gpu_arm(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- training workload (config 5)
+
+def train_arm(args, rank: int, world: int, local_rank: int) -> None:
+    """--workload train: the end-to-end training step of the reference's config 5 -- a random-init Llama-7B
+    decoder (bf16 weights, activation checkpointing per layer), batch 8 x sequence 512 of uniform token ids per
+    rank, ZeroAdamBridge (AdamW, bf16 moments) with its backward hooks reduce-scattering each round of
+    gradients while backward runs, then the fused update + all-gather.  Prints tokens/s for the whole job and
+    the update kernels' share of the step."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from torch.utils.checkpoint import checkpoint
+
+    from adambridge_b200 import native
+    from adambridge_b200.zero import ZeroAdamBridge
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    kern = native.load()
+    dims = dict(LLAMA7B)
+    if args.layers is not None:
+        dims["layers"] = args.layers
+    if args.vocab is not None:
+        dims["vocab"] = args.vocab
+    hidden, vocab, heads = dims["hidden"], dims["vocab"], 32
+    hd = hidden // heads
+    batch, seq = 8, 512
+
+    class RMSNorm(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.weight = torch.nn.Parameter(torch.ones(hidden))
+
+        def forward(self, x):
+            xf = x.float()
+            return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + 1e-5)).to(x.dtype) * self.weight
+
+    class Block(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            lin = lambda o, i: torch.nn.Linear(i, o, bias=False)   # noqa: E731
+            self.q, self.k, self.v, self.o = lin(hidden, hidden), lin(dims["kv"], hidden), lin(dims["kv"], hidden), lin(hidden, hidden)
+            self.gate, self.up, self.down = lin(dims["mlp"], hidden), lin(dims["mlp"], hidden), lin(hidden, dims["mlp"])
+            self.norm1, self.norm2 = RMSNorm(), RMSNorm()
+
+        def forward(self, x, cos, sin):
+            b, t, _ = x.shape
+            h = self.norm1(x)
+
+            def rope(z):
+                z = z.view(b, t, -1, hd).transpose(1, 2)
+                z1, z2 = z[..., : hd // 2], z[..., hd // 2:]
+                return torch.cat((z1 * cos - z2 * sin, z2 * cos + z1 * sin), dim=-1)
+
+            att = F.scaled_dot_product_attention(rope(self.q(h)), rope(self.k(h)),
+                                                 self.v(h).view(b, t, -1, hd).transpose(1, 2), is_causal=True)
+            x = x + self.o(att.transpose(1, 2).reshape(b, t, hidden))
+            h = self.norm2(x)
+            return x + self.down(F.silu(self.gate(h)) * self.up(h))
+
+    class Decoder(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.emb = torch.nn.Embedding(vocab, hidden)
+            self.blocks = torch.nn.ModuleList(Block() for _ in range(dims["layers"]))
+            self.norm = RMSNorm()
+            self.lm_head = torch.nn.Linear(hidden, vocab, bias=False)
+
+        def forward(self, tokens):
+            pos = torch.arange(tokens.shape[1], device=tokens.device, dtype=torch.float32)
+            inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=tokens.device, dtype=torch.float32) / hd))
+            ang = torch.outer(pos, inv)
+            cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+            x = self.emb(tokens)
+            for blk in self.blocks:
+                x = checkpoint(blk, x, cos, sin, use_reentrant=False)
+            return self.lm_head(self.norm(x))
+
+    torch.manual_seed(0)   # the same initial weights on every rank
+    with torch.device(dev):
+        model = Decoder().to(torch.bfloat16)
+    n_params = sum(p.numel() for p in model.parameters())
+    opt = ZeroAdamBridge(list(model.parameters()), lr=2e-5, precision="bf16", rounds=args.rounds,
+                         gather=args.gather).attach_hooks(model)
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    tokens = torch.randint(0, vocab, (batch, seq + 1), device=dev, generator=gen)
+
+    def step():
+        logits = model(tokens[:, :-1])
+        loss = F.cross_entropy(logits.float().reshape(-1, vocab), tokens[:, 1:].reshape(-1))
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches0 = kern.launch_count()
+    opt.trace = []
+    cur = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        t0.record(cur)
+        for _ in range(args.steps):
+            loss = step()
+        t1.record(cur)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    upd_ms = sum(a.elapsed_time(b) for a, b in opt.trace) / args.steps
+    opt.trace = None
+    t = torch.tensor([ms, upd_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, upd_ms = t.tolist()
+    loss_host = float(loss.detach().float().item())
+    if rank != 0:
+        return
+    tokens_per_step = batch * seq * world
+    line = {"metric": "training step tokens/s (Llama-7B decoder, ZeRO-1 AdamW bf16 moments, hooks)",
+            "value": round(tokens_per_step / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "llama-train-c5" if dims == LLAMA7B else f"llama-{dims['layers']}L-train",
+                       "params": n_params, "batch_per_rank": batch, "seq_len": seq, "activation_checkpointing": True,
+                       "hooks": True, "parallelism": f"zero1-dp{world}", "rounds": opt.layout.rounds,
+                       "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None},
+            "update_kernels_ms": round(upd_ms, 3), "loss": round(loss_host, 4),
+            "gpu_launches": kern.launch_count() - launches0, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 
 def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
@@ -442,6 +577,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="abx", choices=["abx", "reference", "reference-gpu"])
+    ap.add_argument("--workload", default="update", choices=["update", "train"],
+                    help="update: the fused optimizer step (the headline); train: config 5's training step")
     ap.add_argument("--algorithm", default="adamw", choices=["adamw", "lion"])
     ap.add_argument("--precision", default="bf16", choices=["fp32", "bf16", "fp8"])
     ap.add_argument("--rounds", type=int, default=8,
@@ -481,7 +618,10 @@ def main() -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        gpu_arm(args, rank, world, local_rank)
+        if args.workload == "train":
+            train_arm(args, rank, world, local_rank)
+        else:
+            gpu_arm(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()
