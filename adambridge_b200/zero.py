@@ -139,6 +139,10 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     all-gather into the update: the weight buffer lives in symmetric memory and the kernel stores each new
     weight into every peer's copy over NVLink; ``'nccl'`` runs NCCL's all-gather round by round instead.
 
+    ``delay_updates`` (after ``delay_warmup_steps`` ordinary steps), as the reference's delayed mode: a step's
+    update writes a second weight buffer and runs while the caller goes on (the next forward), and it becomes
+    the weights at the next step -- the model trains with weights one step stale.  ``flush()`` applies it.
+
     ``step_shard(grad_shard)``: the caller supplies this rank's already reduced gradient shard
     (``shard_numel`` elements, round-major; see :class:`FlatLayout`).  Every parameter is updated every step.
     """
@@ -148,7 +152,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     def __init__(self, params, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 1e-2, *, precision: str = "fp32", master_precision: str = "fp32",
                  stochastic_rounding: bool = True, seed: int = 0, process_group=None, rounds: int | None = None,
-                 max_ctas: int = 0, grad_dtype: torch.dtype | None = None, gather: str = "auto"):
+                 max_ctas: int = 0, grad_dtype: torch.dtype | None = None, gather: str = "auto",
+                 delay_updates: bool = False, delay_warmup_steps: int = 0):
         if not 0.0 <= lr or not 0.0 <= eps or not 0.0 <= weight_decay:
             raise ValueError("lr, eps and weight_decay must be >= 0")
         if not 0.0 <= betas[0] < 1.0 or not 0.0 <= betas[1] < 1.0:
@@ -178,6 +183,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self.grad_dtype = grad_dtype or dtype
         if gather not in ("auto", "p2p", "nccl"):
             raise ValueError("gather must be 'auto', 'p2p' or 'nccl'")
+        if delay_warmup_steps < 0:
+            raise ValueError("delay_warmup_steps must be >= 0")
+        self.delay_updates, self.delay_warmup_steps = bool(delay_updates), int(delay_warmup_steps)
         self._peer_deltas: list[int] | None = None
         numels = [p.numel() for p in self._params]
         flat = None
@@ -211,7 +219,19 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._update_stream = torch.cuda.Stream(dev)
         self._comm_stream = torch.cuda.Stream(dev) if self.world > 1 else None
         self._groups = [native.Group() for _ in self.param_groups]
-        self._segs = self._build_segments()
+        self._seg_objs: list = []
+        self._segs = self._build_segments(self.flat_weights)
+        # delayed updates: the new weights go to a second weight buffer (and, fused, into the peers' second
+        # buffers), which becomes the weights at the next step; allocated at the first delayed step
+        self._shadow: torch.Tensor | None = None
+        self._shadow_segs: list | None = None
+        self._shadow_deltas: list[int] | None = None
+        self._delay_owed = False
+        self._steps_done = 0
+        # reduce-scatter reads of the flat gradients: the last of this step, and the last of the previous step
+        # (which the next writes of the flat gradients wait for)
+        self._grads_read_now: torch.cuda.Event | None = None
+        self._grads_read: torch.cuda.Event | None = None
         self.trace: list | None = None   # (start, end) CUDA events of every update launch, when a list
         self.norm_trace: list = []       # (start, end) events of the norm kernels, while ``trace`` is a list
         self.release_grads = True
@@ -251,17 +271,16 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     # ------------------------------------------------------------------ segments
 
-    def _build_segments(self) -> list[ctypes.Array]:
-        """One segment array per round, pointing into this rank's state and the flat weights."""
+    def _build_segments(self, weights: torch.Tensor) -> list[ctypes.Array]:
+        """One segment array per round, pointing into this rank's state and the flat weight buffer ``weights``."""
         p_hi, p_lo = self.master.native_buffers
         m_buf, m_scale = self.m.native_buffers
         v_buf, v_scale = (None, None) if self.v is None else self.v.native_buffers
         p_es = p_hi.element_size()
         m_es = m_buf.element_size()
-        out_es = self.flat_weights.element_size()
+        out_es = weights.element_size()
         g_es = self.grad_shard.element_size()
         rounds = []
-        self._seg_objs = []
         for pieces in self._pieces:
             ptrs = []
             for pc in pieces:
@@ -276,7 +295,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 if v_buf is not None:
                     s.v = v_buf.data_ptr() + pc.local_lo * m_es
                     s.v_scale = v_scale.data_ptr() + 4 * (pc.local_lo // ALIGN) if v_scale is not None else None
-                s.out = self.flat_weights.data_ptr() + pc.flat_lo * out_es
+                s.out = weights.data_ptr() + pc.flat_lo * out_es
                 s.out_dtype = native.dtype_code_of(self.dtype)
                 s.n = pc.n
                 s.offset = pc.t_lo
@@ -288,6 +307,52 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 ptrs.append(ctypes.pointer(s))
             rounds.append(self.kernels.segment_array(ptrs))
         return rounds
+
+    # ------------------------------------------------------------------ delayed updates
+
+    def _delayed(self) -> bool:
+        return self.delay_updates and self._steps_done >= self.delay_warmup_steps
+
+    def _ensure_shadow(self) -> None:
+        """The second weight buffer (symmetric like the first when the all-gather is fused); collective on first
+        use, which every rank reaches at the same step."""
+        if self._shadow is not None:
+            return
+        L = self.layout
+        with torch.no_grad(), torch.cuda.device(self.device):
+            if self._peer_deltas is not None:
+                import torch.distributed._symmetric_memory as symm
+                self._shadow = symm.empty(L.total, dtype=self.dtype, device=self.device)
+                self._shadow.zero_()
+                self._symm_shadow = symm.rendezvous(self._shadow, group=self.pg)
+                ptrs = [int(x) for x in self._symm_shadow.buffer_ptrs]
+                self._shadow_deltas = [ptrs[r] - ptrs[self.rank] for r in range(self.world) if r != self.rank]
+            else:
+                self._shadow = torch.zeros(L.total, dtype=self.dtype, device=self.device)
+        self._shadow_segs = self._build_segments(self._shadow)
+
+    def _apply_pending(self, cur) -> None:
+        """The previous step's delayed update becomes the weights (on ``cur``, after that update and its gather)."""
+        if not self._delay_owed:
+            return
+        cur.wait_stream(self._update_stream)
+        if self._comm_stream is not None:
+            cur.wait_stream(self._comm_stream)
+        with torch.no_grad():
+            self.flat_weights.copy_(self._shadow)
+        self._delay_owed = False
+
+    def _after_grad_reads(self, stream) -> None:
+        """``stream`` waits until the previous step's last reduce-scatter has read the flat gradients (a delayed
+        step returns before it ran, and the next backward writes the flat gradients again)."""
+        if self._grads_read is not None:
+            stream.wait_event(self._grads_read)
+            self._grads_read = None
+
+    @torch.no_grad()
+    def flush(self) -> None:
+        """Apply a pending delayed update to the parameters (before evaluating or saving)."""
+        self._apply_pending(torch.cuda.current_stream(self.device))
 
     def _refresh(self) -> None:
         """Step number and group hyperparameters (re-read every step, so LR schedulers work)."""
@@ -313,6 +378,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         """Every parameter's local gradient in the flat gradient buffer (no copy where p.grad views it)."""
         L = self.layout
         flat = self._flat_grad_buffer()
+        self._after_grad_reads(torch.cuda.current_stream(self.device))
         for i, p in enumerate(self._params):
             if p.grad is None:
                 raise RuntimeError(f"parameter {i} has no gradient: ZeRO steps update every parameter")
@@ -381,10 +447,10 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         if not self._hooked:
             return
         L = self.layout
-        self._pending = [0] * L.rounds
+        self._round_waiting = [0] * L.rounds
         for rounds in self._rounds_of:
             for r in rounds:
-                self._pending[r] += 1
+                self._round_waiting[r] += 1
         self._arrived = [False] * len(self._params)
         self._reduced = [False] * L.rounds
 
@@ -394,13 +460,14 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             raise RuntimeError("ZeroAdamBridge: parameter received a second gradient before step()")
         self._arrived[i] = True
         a, b = self.layout.flat_slice(i)
+        self._after_grad_reads(torch.cuda.current_stream(self.device))
         with torch.no_grad():
             self._flat_grad_buffer()[a:b].copy_(p.grad.reshape(-1))
         if self.release_grads:
             p.grad = None
         for r in self._rounds_of[i]:
-            self._pending[r] -= 1
-            if self._pending[r] == 0:
+            self._round_waiting[r] -= 1
+            if self._round_waiting[r] == 0:
                 self._reduce_round(r)
 
     def _reduce_round(self, r: int) -> None:
@@ -416,11 +483,19 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 self._update_stream.wait_stream(cur)
                 with torch.cuda.stream(self._update_stream):
                     shard.copy_(src)
+                    self._record_grad_reads(self._update_stream)
             else:
                 self._comm_stream.wait_stream(cur)
+                self._comm_stream.wait_stream(self._update_stream)   # a delayed update may still read the shard
                 with torch.cuda.stream(self._comm_stream):
                     dist.reduce_scatter_tensor(shard, src, op=dist.ReduceOp.AVG, group=self.pg)
+                    self._record_grad_reads(self._comm_stream)
         self._reduced[r] = True
+
+    def _record_grad_reads(self, stream) -> None:
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._grads_read_now = ev
 
     def _finish_hooked_reduce(self) -> None:
         """Before the update of a hooked step: every parameter's gradient arrived; the update stream waits for
@@ -449,6 +524,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                                         or weights_out.dtype != self.dtype):
             raise ValueError(f"weights_out must be a host tensor of {L.shard_numel} {self.dtype} elements")
         if grad_shard is not None and host_in is None and grad_shard.data_ptr() != self.grad_shard.data_ptr():
+            self._apply_pending(torch.cuda.current_stream(self.device))   # a delayed update may still read it
             self.grad_shard.copy_(grad_shard)
         if self._clip_coef is not None:
             if host_in is not None:
@@ -507,13 +583,16 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 with torch.cuda.stream(upd):
                     for r in range(L.rounds):
                         self.grad_shard[r * L.chunk:(r + 1) * L.chunk].copy_(flat[slice(*L.round_range(r))])
+                    self._record_grad_reads(upd)
             else:
                 comm.wait_stream(cur)
+                comm.wait_stream(upd)   # a delayed update may still read the shard
                 with torch.cuda.stream(comm):
                     for r in range(L.rounds):
                         dist.reduce_scatter_tensor(self.grad_shard[r * L.chunk:(r + 1) * L.chunk],
                                                    flat[slice(*L.round_range(r))], op=dist.ReduceOp.AVG,
                                                    group=self.pg)
+                    self._record_grad_reads(comm)
                 upd.wait_stream(comm)
         return self._clip_shard(max_norm, cur)
 
@@ -523,6 +602,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         the ranks hold (``grad_shard``, default ``self.grad_shard``); the next ``step_shard()`` applies the clip."""
         cur = torch.cuda.current_stream(self.device)
         if grad_shard is not None and grad_shard.data_ptr() != self.grad_shard.data_ptr():
+            self._apply_pending(cur)   # a delayed update may still read the shard
             self.grad_shard.copy_(grad_shard)
         self._update_stream.wait_stream(cur)
         return self._clip_shard(max_norm, cur)
@@ -553,8 +633,16 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     def _run(self, flat_grads: torch.Tensor | None, g_scale: torch.Tensor | None = None,
              synced: bool = False, host_in: torch.Tensor | None = None, host_out: torch.Tensor | None = None) -> None:
         L = self.layout
-        self._refresh()
         cur = torch.cuda.current_stream(self.device)
+        had_pending = self._delay_owed
+        self._apply_pending(cur)        # delayed: the previous step's update becomes the weights now
+        delayed = self._delayed()
+        if delayed:
+            self._ensure_shadow()
+        weights = self._shadow if delayed else self.flat_weights
+        segs = self._shadow_segs if delayed else self._segs
+        deltas = self._shadow_deltas if delayed else self._peer_deltas
+        self._refresh()
         upd, comm = self._update_stream, self._comm_stream
         p2p = self._peer_deltas is not None
         upd.wait_stream(cur)
@@ -568,7 +656,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             h2d.wait_stream(cur)
             d2h.wait_stream(cur)
         with torch.cuda.device(self.device):
-            if p2p and flat_grads is None and not synced:
+            if p2p and (delayed or had_pending or (flat_grads is None and not synced)):
                 self._barrier(upd)   # no peer still reads the weights this update overwrites
             for r in range(L.rounds):
                 if host_in is not None:
@@ -580,21 +668,23 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                     shard = self.grad_shard[r * L.chunk:(r + 1) * L.chunk]
                     src = flat_grads[slice(*L.round_range(r))]
                     if comm is None:
-                        shard.copy_(src)
+                        with torch.cuda.stream(upd):   # in order with the update that reads it
+                            shard.copy_(src)
+                            self._record_grad_reads(upd)
                     else:
                         with torch.cuda.stream(comm):
                             dist.reduce_scatter_tensor(shard, src, op=dist.ReduceOp.AVG, group=self.pg)
+                            self._record_grad_reads(comm)
                         upd.wait_stream(comm)
                 start = end = None
                 if self.trace is not None:
                     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     start.record(upd)
-                if len(self._segs[r]):
+                if len(segs[r]):
                     if p2p:
-                        self.kernels.multi_step_replicated(upd, self._segs[r], self._peer_deltas, self.max_ctas,
-                                                           g_scale)
+                        self.kernels.multi_step_replicated(upd, segs[r], deltas, self.max_ctas, g_scale)
                     else:
-                        self.kernels.multi_step(upd, self._segs[r], self.max_ctas, g_scale)
+                        self.kernels.multi_step(upd, segs[r], self.max_ctas, g_scale)
                 if end is not None:
                     end.record(upd)
                     self.trace.append((start, end))
@@ -602,18 +692,24 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                     d2h.wait_stream(upd)
                     with torch.cuda.stream(d2h):
                         host_out[r * L.chunk:(r + 1) * L.chunk].copy_(
-                            self.flat_weights[slice(*L.rank_range(r, self.rank))], non_blocking=True)
+                            weights[slice(*L.rank_range(r, self.rank))], non_blocking=True)
                 if comm is not None and not p2p:
                     comm.wait_stream(upd)
                     with torch.cuda.stream(comm):
-                        out = self.flat_weights[slice(*L.round_range(r))]
-                        mine = self.flat_weights[slice(*L.rank_range(r, self.rank))]
+                        out = weights[slice(*L.round_range(r))]
+                        mine = weights[slice(*L.rank_range(r, self.rank))]
                         dist.all_gather_into_tensor(out, mine, group=self.pg)
         if p2p:
             self._barrier(upd)       # every peer's stores into this rank's weights have landed
-        cur.wait_stream(upd)
-        if comm is not None:
-            cur.wait_stream(comm)
+        self._steps_done += 1
+        self._grads_read, self._grads_read_now = self._grads_read_now, None
+        if delayed:
+            # the update overlaps whatever the caller runs next; the next step (or flush) makes it the weights
+            self._delay_owed = True
+        else:
+            cur.wait_stream(upd)
+            if comm is not None:
+                cur.wait_stream(comm)
         if h2d is not None:
             cur.wait_stream(h2d)
             cur.wait_stream(d2h)
@@ -679,6 +775,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         moments, assembled from every rank's shard into host tensors -- loadable by ``AdamBridge`` and by a
         ZeRO optimizer of any world size.  Collective: every rank of the group must call it.  With
         ``rank0_only`` the other ranks take part in the gathers and return an empty ``state``."""
+        self.flush()
         torch.cuda.current_stream(self.device).wait_stream(self._update_stream)
         sd = super().state_dict()
         sd["state"] = {}
@@ -730,6 +827,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             raise ValueError(f"checkpoint parameters are at different steps {sorted(steps)}; ZeRO needs one")
         super().load_state_dict({"state": {}, "param_groups": state_dict["param_groups"]})
         dev = self.device
+        torch.cuda.synchronize(dev)
+        self._delay_owed = False          # a delayed update in flight is superseded by the loaded state
         runs = {}
         for unit, padded in ((1, False), (1, True), (ALIGN, True)):
             for index, p_lo, s_lo, length in L.shard_runs(self.rank, unit, padded):

@@ -259,7 +259,8 @@ def reference_gpu_arm(args, rank: int) -> None:
 # --------------------------------------------------------------------------- training workload (config 5)
 
 def train_arm(args, rank: int, world: int, local_rank: int) -> None:
-    """--workload train: the end-to-end training step of the reference's config 5 -- a random-init Llama-7B
+    """--workload train: the end-to-end training step of the reference's config 5 (with ``--delay``, its
+    delayed-update variant) -- a random-init Llama-7B
     decoder (bf16 weights, activation checkpointing per layer), batch 8 x sequence 512 of uniform token ids per
     rank, ZeroAdamBridge (AdamW, bf16 moments) with its backward hooks reduce-scattering each round of
     gradients while backward runs, then the fused update + all-gather.  Prints tokens/s for the whole job and
@@ -339,7 +340,7 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> None:
         model = Decoder().to(torch.bfloat16)
     n_params = sum(p.numel() for p in model.parameters())
     opt = ZeroAdamBridge(list(model.parameters()), lr=2e-5, precision="bf16", rounds=args.rounds,
-                         gather=args.gather).attach_hooks(model)
+                         gather=args.gather, delay_updates=args.delay).attach_hooks(model)
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     tokens = torch.randint(0, vocab, (batch, seq + 1), device=dev, generator=gen)
 
@@ -384,7 +385,8 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "llama-train-c5" if dims == LLAMA7B else f"llama-{dims['layers']}L-train",
                        "params": n_params, "batch_per_rank": batch, "seq_len": seq, "activation_checkpointing": True,
-                       "hooks": True, "parallelism": f"zero1-dp{world}", "rounds": opt.layout.rounds,
+                       "hooks": True, "delay_updates": args.delay, "parallelism": f"zero1-dp{world}",
+                       "rounds": opt.layout.rounds,
                        "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None},
             "update_kernels_ms": round(upd_ms, 3), "loss": round(loss_host, 4),
             "gpu_launches": kern.launch_count() - launches0, "clocks": clocks.summary()}
@@ -590,6 +592,8 @@ def main() -> int:
     ap.add_argument("--vocab", type=int, default=None, help="override the vocabulary (small profiling cases)")
     ap.add_argument("--clip", type=float, default=None,
                     help="clip_grad_norm_ to this max norm before every step (norm kernels + scaled update)")
+    ap.add_argument("--delay", action="store_true",
+                    help="--workload train: delayed updates (each update overlaps the next forward)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")

@@ -375,3 +375,90 @@ def test_zero_host_streamed_step_equals_device_step():
     assert torch.equal(out, mine)
     with pytest.raises(ValueError):
         ob.step_shard(g[:-1])
+
+
+# ---------------------------------------------------------------------------------------------- delayed updates
+
+def _delayed_run(opt, model, steps, rank, device, hooks):
+    if hooks:
+        opt.attach_hooks(model)
+    for step in range(1, steps + 1):
+        _mlp_loss(model, step, rank, device).backward()
+        opt.step()
+        opt.zero_grad()
+    opt.flush()
+    torch.cuda.synchronize()
+    return [p.detach().cpu() for p in model.parameters()]
+
+
+@pytest.mark.parametrize("warmup", [0, 2])
+@pytest.mark.parametrize("hooks", [False, True])
+def test_zero_delayed_updates_equal_adambridge_delayed(warmup, hooks):
+    """delay_updates: each step's update lands one step late, as in AdamBridge's (the reference's) delayed mode --
+    identical weights after flush(), with and without backward hooks, with and without warm-up steps."""
+    ma, mb = _mlp_pair("cuda")
+    oa = ab.AdamBridge(list(ma.parameters()), lr=2e-3, precision="bf16", seed=3, small_param_threshold=0,
+                       delay_updates=True, delay_warmup_steps=warmup)
+    ob = ZeroAdamBridge(list(mb.parameters()), lr=2e-3, precision="bf16", seed=3, rounds=3,
+                        delay_updates=True, delay_warmup_steps=warmup)
+    want = _delayed_run(oa, ma, 5, 0, "cuda", False)
+    got = _delayed_run(ob, mb, 5, 0, "cuda", hooks)
+    assert all(torch.equal(a, b) for a, b in zip(got, want))
+    oa.close()
+
+
+def test_zero_delayed_weights_lag_one_step():
+    """Before flush() the parameters hold the previous step's update: after two delayed steps they equal a
+    synchronous optimizer's after one step on the same gradients."""
+    ma, mb = _mlp_pair("cuda")
+    o_sync = ZeroAdamBridge(list(ma.parameters()), lr=2e-3, precision="bf16", seed=3, rounds=2)
+    o_del = ZeroAdamBridge(list(mb.parameters()), lr=2e-3, precision="bf16", seed=3, rounds=2, delay_updates=True)
+    grads = []
+    for step in (1, 2):
+        g = torch.Generator().manual_seed(step)
+        grads.append([(torch.randn(p.shape, generator=g) * 1e-2).to("cuda", torch.bfloat16) for p in ma.parameters()])
+    for p, g in zip(ma.parameters(), grads[0]):
+        p.grad = g
+    o_sync.step()
+    after_one = [p.detach().clone() for p in ma.parameters()]
+    for gs in grads:
+        for p, g in zip(mb.parameters(), gs):
+            p.grad = g
+        o_del.step()
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, b) for a, b in zip(mb.parameters(), after_one))
+    o_del.flush()
+    assert not all(torch.equal(a, b) for a, b in zip(mb.parameters(), after_one))
+
+
+def _delayed_rank(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        dev = f"cuda:{rank}"
+        ma, mb = _mlp_pair(dev)
+        kw = dict(lr=2e-3, precision="bf16", seed=3, rounds=3, delay_updates=True)
+        oa = ZeroAdamBridge(list(ma.parameters()), gather="p2p", **kw)
+        ob = ZeroAdamBridge(list(mb.parameters()), gather="nccl", **kw)
+        got = _delayed_run(oa, ma, 4, rank, dev, True)
+        want = _delayed_run(ob, mb, 4, rank, dev, False)
+        with open(os.path.join(out_dir, f"delayed{rank}.pkl"), "wb") as f:
+            pickle.dump((got, want), f)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_zero_two_gpus_delayed_updates():
+    """2 ranks, delayed updates: the fused peer-store gather with hooks and NCCL's gather with step() end with the
+    same weights on every rank."""
+    import tempfile
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_delayed_rank, args=(2, _free_port(), tmp), nprocs=2, start_method="spawn", join=True)
+        ranks = [pickle.load(open(os.path.join(tmp, f"delayed{r}.pkl"), "rb")) for r in range(2)]
+    for got, want in ranks:
+        assert all(torch.equal(a, b) for a, b in zip(got, want))
+    assert all(torch.equal(a, b) for a, b in zip(ranks[0][0], ranks[1][0]))
