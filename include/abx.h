@@ -215,10 +215,13 @@ int abx_clip_coef(void* stream, const abx_tensor* grads, int32_t n, float max_no
                   float* total_coef, void* workspace, size_t workspace_bytes);
 
 /* abx_clip_coef without a caller workspace.  No counterpart in the reference (adambridge has no
- * device-side norm: its callers run torch.nn.utils.clip_grad_norm_).  The per-tile partial sums
- * live in a static device array inside this library (2 MiB per device), so the call allocates
- * nothing: no cudaMalloc, no caller buffer beyond its outputs sq, norms (may be NULL) and
- * total_coef, whose meaning is abx_clip_coef's.
+ * device-side norm: its callers run torch.nn.utils.clip_grad_norm_).  For callers that cannot
+ * allocate device memory: a C or FFI host that only holds the device pointers a framework gave it
+ * and has no CUDA allocator of its own, or a training loop that reserved its device memory up
+ * front and must not allocate per step (an allocation there can fail or fragment the pool).  The
+ * per-tile partial sums live in a static device array inside this library (2 MiB on every device
+ * that loads it, held until exit), so the call allocates nothing: no cudaMalloc, no caller buffer
+ * beyond its outputs sq, norms (may be NULL) and total_coef, whose meaning is abx_clip_coef's.
  *   Limit: the gradients' 16384-element tiles, the sum of ceil(n_i / 16384), must number at most
  *   524,288 (about 8.59e9 elements); more is rejected before anything runs, with ABX_E_SCRATCH
  *   and a message in abx_last_error().

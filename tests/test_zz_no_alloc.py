@@ -1,7 +1,8 @@
-"""abx_clip_coef_noalloc (the clip entry point whose scratch is a static device array in libabx) against
-abx_clip_coef (caller workspace): the same sums of squares, norms, total norm and coefficient, bit for bit,
-over two calls in a row -- the second call reuses the static scratch the first one wrote.  Collected last
-(file name), so it also runs after every other GPU test in the same process."""
+"""abx_clip_coef_noalloc -- the clip entry point for callers that cannot allocate device memory (a C or FFI host
+without a CUDA allocator of its own, or a loop that must not allocate per step), whose scratch is a static
+device array in libabx -- against abx_clip_coef (caller workspace): the same sums of squares, norms, total norm
+and coefficient, bit for bit, over two calls in a row; the second call reuses the static scratch the first one
+wrote.  Collected last (file name), so it also runs after every other GPU test in the same process."""
 
 from __future__ import annotations
 
