@@ -89,6 +89,28 @@ def test_grad_scale_bit_exact(kernels, oracle):
     assert not bad, bad[:5]
 
 
+@pytest.mark.parametrize("sr", [1, 0])
+def test_offsets_past_32_bits_bit_exact(kernels, oracle, sr):
+    """Element offsets at and beyond 2^32 (a piece deep inside a huge tensor): the rounding streams index
+    elements by the offset plus position modulo 2^32, as the reference does (csrc:100-106, 1577), so a piece
+    whose indices wrap around 2^32 during the segment, and odd offsets (no 4-aligned hash groups) where the
+    moments are not FP8, all match the oracle -- in partial tiles and in staged whole tiles."""
+    cases = []
+    k = 0
+    for algo, mv, pt in itertools.product(ALGOS, MOMENTS, MASTERS):
+        offsets = [(1 << 32) - 1024, (1 << 40) + (1 << 31) - 896, (1 << 33) + 384]
+        if mv != O.DT_FP8:
+            offsets += [(1 << 32) - 3, (1 << 35) + 1]
+        for off in offsets:
+            for n in (3000, 70001):
+                hs = O.HostSegment.random(n, O.DT_BF16, mv, O.DT_BF16, pt, algo, seed=500 + k, offset=off, index=k)
+                hs.randomize_moments(900 + k)
+                cases.append((hs, f"algo={algo} mv={mv} p={pt} offset={off} n={n}"))
+                k += 1
+    bad = [(d, m) for d, m in _run_steps(cases, kernels, oracle, O.SIMD_AVX512, sr=sr) if m]
+    assert not bad, f"{len(bad)} cases differ, e.g. {bad[:5]}"
+
+
 def test_capped_grid_bit_exact(kernels, oracle):
     """max_ctas only changes which CTA takes which tile, never a result."""
     cases = _cases(seed0=3, sizes=(100003,))
