@@ -723,7 +723,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     def memory_report(self) -> dict[str, int]:
         rep = {"master": self.master.nbytes, "moments": self.m.nbytes + (self.v.nbytes if self.v is not None else 0),
                "grad_shard": self.grad_shard.nbytes, "weights": self.flat_weights.nbytes,
-               "delayed_weights": 0 if self._shadow is None else self._shadow.nbytes}
+               "delayed_weights": 0 if self._shadow is None else self._shadow.nbytes,
+               "flat_grads": 0 if self._flat_grads is None else self._flat_grads.nbytes}
         rep["total"] = sum(rep.values())
         return rep
 
