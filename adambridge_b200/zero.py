@@ -108,6 +108,13 @@ class FlatLayout:
     def flat_slice(self, index: int) -> tuple[int, int]:
         return self.offsets[index], self.offsets[index] + self.numels[index]
 
+    def rounds_of(self, index: int) -> list[int]:
+        """The rounds whose flat range holds elements of parameter ``index`` (an empty parameter: the round of
+        its offset), in order -- the reduce-scatters its gradient takes part in."""
+        a, b = self.flat_slice(index)
+        span = self.world * self.chunk
+        return list(range(a // span, (max(b, a + 1) - 1) // span + 1))
+
     def shard_runs(self, rank: int, unit: int = 1, padded: bool = False) -> list[tuple[int, int, int, int]]:
         """``(index, param_lo, shard_lo, length)`` for every piece of ``rank``'s shard, in entries of an array
         holding one entry per ``unit`` elements (1: weights, master, moments; 128: FP8 block scales).
@@ -423,11 +430,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             return self
         wanted = None if model is None else {id(p) for p in model.parameters()}
         L = self.layout
-        self._rounds_of = []
-        for i in range(len(self._params)):
-            a, b = L.flat_slice(i)
-            span = L.world * L.chunk
-            self._rounds_of.append(list(range(a // span, (max(b, a + 1) - 1) // span + 1)))
+        self._rounds_of = [L.rounds_of(i) for i in range(len(self._params))]
         hook = torch.compiler.disable(self._on_grad_ready)
         self._index_of = {id(p): i for i, p in enumerate(self._params)}
         for p in self._params:

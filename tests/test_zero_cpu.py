@@ -51,6 +51,22 @@ def test_one_round_without_peers():
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])
+@pytest.mark.parametrize("rounds", [None, 1, 4, 16])
+def test_rounds_of_lists_exactly_the_rounds_a_parameter_touches(world, rounds):
+    """The backward hooks start a round's reduce-scatter when every parameter listed for it has its gradient:
+    rounds_of must list exactly the rounds whose flat range intersects the parameter, and every piece of a
+    rank's shard must belong to a parameter listed for that piece's round."""
+    L = FlatLayout(SIZES, world, rounds)
+    for i in range(len(SIZES)):
+        a, b = L.flat_slice(i)
+        want = [r for r in range(L.rounds) if max(a, L.round_range(r)[0]) < min(b, L.round_range(r)[1])]
+        assert L.rounds_of(i) == want
+    for rank in range(world):
+        for r, pieces in enumerate(L.pieces(rank)):
+            assert all(r in L.rounds_of(pc.index) for pc in pieces)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
 @pytest.mark.parametrize("rounds", [None, 1, 4])
 @pytest.mark.parametrize("unit,padded", [(1, False), (1, True), (ALIGN, True)])
 def test_shard_runs_scatter_and_gather_round_trip(world, rounds, unit, padded):
