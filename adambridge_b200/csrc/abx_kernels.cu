@@ -274,7 +274,9 @@ __device__ __forceinline__ void grad4(const KSeg& S, int64_t i0, int cnt, const 
         ld4_f32(static_cast<const float*>(S.g) + i0, reinterpret_cast<const float*>(s), cnt, S.vec_ok, g);
     }
     if (gs != nullptr) {
-        const float f = *gs;
+        // a bf16 gradient is scaled as torch scales a bf16 CUDA tensor in place by an fp32 scalar tensor:
+        // by the scalar rounded to bf16, the product rounded back to bf16
+        const float f = GT == ABX_DT_BF16 ? u2f(bf16_rne(f2u(*gs)) & 0xffff0000U) : *gs;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             g[k] = __fmul_rn(g[k], f);
@@ -657,7 +659,9 @@ __device__ __forceinline__ void fast_grad4(const uint8_t* s, const float* gs, fl
     if constexpr (GT == ABX_DT_BF16) lds_b16x4(s, g);
     else lds_f32x4(s, g);
     if (gs != nullptr) {
-        const float f = *gs;
+        // a bf16 gradient is scaled as torch scales a bf16 CUDA tensor in place by an fp32 scalar tensor:
+        // by the scalar rounded to bf16, the product rounded back to bf16
+        const float f = GT == ABX_DT_BF16 ? u2f(bf16_rne(f2u(*gs)) & 0xffff0000U) : *gs;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             g[k] = __fmul_rn(g[k], f);

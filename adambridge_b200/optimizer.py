@@ -298,7 +298,8 @@ class AdamBridge(torch.optim.Optimizer):
         coefficient inside the update kernel, rounding to the gradient's dtype exactly as torch's in-place
         multiply does, so ``opt.clip_grad_norm_(c); opt.step()`` equals ``clip_grad_norm_(params, c); opt.step()``.
         The norms come from libabx's multi-tensor norm kernels (one read of the gradients).  Only the L2 norm is
-        fused; all gradients must share one dtype.  ``error_if_nonfinite`` synchronizes to check the norm."""
+        fused; bf16 and fp32 gradients may be mixed (norms rounded per dtype, the total in fp32, as torch does).
+        ``error_if_nonfinite`` synchronizes to check the norm."""
         del foreach
         if float(norm_type) != 2.0:
             raise ValueError("AdamBridge.clip_grad_norm_ computes the L2 norm (norm_type=2) only")

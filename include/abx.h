@@ -157,8 +157,9 @@ int abx_hparams_for(const abx_segment* seg, abx_hparams* out);
  *   caller-supplied coefficients hps[i] for segs[i]; groups and steps are ignored.
  * abx_multi_step_scaled / abx_multi_apply_scaled: as above, and every gradient
  *   element is first multiplied by the device scalar *g_scale (gradient clipping
- *   or loss unscaling fused into the update); a bf16 gradient is rounded back to
- *   bf16 after the multiply, as an in-place torch multiply would leave it.
+ *   or loss unscaling fused into the update), as an in-place torch multiply of
+ *   the CUDA gradient by an fp32 scalar tensor leaves it: a bf16 gradient is
+ *   multiplied by *g_scale rounded to bf16, and the product rounded to bf16.
  *   g_scale NULL means 1.  Not in the reference: its callers scale the
  *   gradient in place before calling it.
  */

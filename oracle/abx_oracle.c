@@ -219,13 +219,19 @@ static float lion_elem(float p, float g, float* m, const abx_hparams* h)
 }
 
 /* The gradient as the update sees it: optionally multiplied by a clip / unscale
- * factor, rounded back to bf16 for a bf16 gradient (torch's in-place multiply). */
+ * factor as torch's in-place multiply of a CUDA tensor by an fp32 scalar tensor
+ * does it -- for a bf16 gradient, by the factor rounded to bf16, and the product
+ * rounded back to bf16. */
 static float grad_elem(const abx_segment* s, int64_t i, const float* g_scale)
 {
     float g = load_elem(s->g, s->g_dtype, i);
     if (g_scale) {
-        g = g * *g_scale;
-        if (s->g_dtype == ABX_DT_BF16) g = u2f(bf16_rne_bits(f2u(g)) & 0xffff0000U);
+        if (s->g_dtype == ABX_DT_BF16) {
+            const float f = u2f(bf16_rne_bits(f2u(*g_scale)) & 0xffff0000U);
+            g = u2f(bf16_rne_bits(f2u(g * f)) & 0xffff0000U);
+        } else {
+            g = g * *g_scale;
+        }
     }
     return g;
 }

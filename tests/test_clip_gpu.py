@@ -92,10 +92,58 @@ def test_non_finite_gradient_gives_torch_coefficient():
     assert coef.item() == want_coef.item() == 0.0
 
 
-def test_mixed_dtypes_rejected():
-    grads = _grads([10], torch.bfloat16) + _grads([10], torch.float32)
-    with pytest.raises(ValueError, match="one dtype"):
-        clip_coefficient(grads, 1.0)
+def test_mixed_dtypes_follow_torch():
+    """bf16 and fp32 gradients together (a bf16 model whose norms stay fp32): each norm in its gradient's dtype,
+    the total in fp32 over all of them, as torch's clip_grad_norm_ groups them."""
+    grads = _grads([4096, 300, 65536], torch.bfloat16, seed=3) + _grads([896, 70_000], torch.float32, seed=4)
+    total, coef, norms = clip_coefficient(grads, 0.05)
+    want_total, want_coef = _torch_total_and_coef(grads, 0.05)
+    assert total.dtype == want_total.dtype == torch.float32
+    torch.testing.assert_close(total, want_total, rtol=1e-6, atol=0.0)
+    torch.testing.assert_close(coef, want_coef.reshape(1), rtol=2e-6, atol=0.0)
+    want_norms = [torch.linalg.vector_norm(g, 2.0).float() for g in grads]
+    torch.testing.assert_close(norms, torch.stack(want_norms), rtol=1e-6, atol=0.0)
+    assert all(norms[i].item() == norms[i].to(torch.bfloat16).float().item() for i in range(3))
+
+
+class _MixedNet(torch.nn.Module):
+    """bf16 linear layers with an fp32 norm weight between them."""
+
+    def __init__(self):
+        super().__init__()
+        self.a = torch.nn.Linear(128, 256).to(torch.bfloat16)
+        self.norm = torch.nn.LayerNorm(256)
+        self.b = torch.nn.Linear(256, 64).to(torch.bfloat16)
+
+    def forward(self, x):
+        return self.b(self.norm(self.a(x).float()).to(torch.bfloat16))
+
+
+def test_fused_clip_with_mixed_dtypes_applies_its_coefficient():
+    """opt.clip_grad_norm_ + step() on a mixed bf16/fp32 model == scaling the gradients in place by the same
+    coefficient (torch's _foreach_mul_, as clip_grad_norm_ scales them) then step(), bit for bit."""
+    results = []
+    for fused in (True, False):
+        torch.manual_seed(0)
+        model = _MixedNet().cuda()
+        opt = ab.AdamBridge(model.parameters(), lr=3e-3, precision="bf16", small_param_threshold=100)
+        for step in range(3):
+            x = torch.randn(32, 128, device="cuda", generator=torch.Generator(device="cuda").manual_seed(step))
+            model(x.to(torch.bfloat16)).float().square().mean().backward()
+            grads = [p.grad for p in model.parameters()]
+            if fused:
+                opt.clip_grad_norm_(0.02)
+            else:
+                _, coef, _ = clip_coefficient(grads, 0.02)
+                for dtype in (torch.bfloat16, torch.float32):
+                    group = [g for g in grads if g.dtype == dtype]
+                    torch._foreach_mul_(group, coef[0])
+            opt.step()
+            opt.zero_grad()
+        torch.cuda.synchronize()
+        results.append([p.detach().clone() for p in model.parameters()])
+        opt.close()
+    assert all(torch.equal(a, b) for a, b in zip(*results))
 
 
 class _Net(torch.nn.Module):
