@@ -294,8 +294,11 @@ ABX_API int abx_clip_coef(void* stream, const abx_tensor* grads, int32_t n, floa
 // The per-tile partial sums live in a file-scope __device__ array of kNoAllocTiles floats (2 MiB per
 // device, enough for 524,288 tiles of 16384 elements: about 8.59e9 gradient elements), so a call
 // needs no caller workspace and allocates nothing, on the device or the host.  The array's device
-// address is looked up once per device, with that device current, on the first call there (this is
-// also when the module's device code is loaded): make that first call before any stream capture.
+// address is looked up with the device current on the first call in a CUDA context (this is also when
+// the module's device code is loaded there): make that first call before any stream capture.  The
+// address is kept per device together with the context it belongs to, and looked up again when the
+// calling thread's context is another one (after cudaDeviceReset, or under a context that is not the
+// device's primary one), where the module is loaded again, at another address.
 // Every partial that a call reads was written earlier in the same call, so nothing needs to start at
 // zero.  All calls on one device share the array: calls whose work overlaps on the device (issued
 // to two streams, or from two host threads without ordering) race on it.
@@ -305,8 +308,39 @@ constexpr int kNoAllocDevices = 64;
 
 __device__ __align__(256) float g_noalloc_partials[kNoAllocTiles];
 
+struct NoAllocSlot {
+    unsigned long long ctx = 0;   // unique id of the context the address belongs to
+    float* addr = nullptr;
+};
+
 static std::mutex g_noalloc_mu;
-static float* g_noalloc_addr[kNoAllocDevices];
+static NoAllocSlot g_noalloc[kNoAllocDevices];
+
+// The unique id of the calling thread's current CUDA context (0: none current yet, or the driver does not
+// report ids), through driver entry points the runtime resolves -- the library does not link libcuda.
+static unsigned long long current_context_id()
+{
+    using GetCurrent = int (*)(void**);
+    using GetId = int (*)(void*, unsigned long long*);
+    static std::once_flag once;
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(f);
+    });
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+    return id;
+}
 
 static int noalloc_scratch(float** out)
 {
@@ -316,13 +350,16 @@ static int noalloc_scratch(float** out)
     if (dev < 0 || dev >= kNoAllocDevices)
         return abx::set_error("abx_clip_coef_noalloc: device index out of range", cudaErrorInvalidDevice);
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
+    NoAllocSlot& slot = g_noalloc[dev];
+    const unsigned long long ctx = current_context_id();
+    if (!slot.addr || ctx == 0 || slot.ctx != ctx) {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        e = cudaGetSymbolAddress(&p, g_noalloc_partials);   // with the device current; loads the module
         if (e != cudaSuccess) return abx::set_error("abx_clip_coef_noalloc: cudaGetSymbolAddress", e);
-        g_noalloc_addr[dev] = static_cast<float*>(p);
+        slot.addr = static_cast<float*>(p);
+        slot.ctx = current_context_id();                     // current now, if it was not before
     }
-    *out = g_noalloc_addr[dev];
+    *out = slot.addr;
     return ABX_OK;
 }
 

@@ -32,10 +32,7 @@ BYTES_PER_PARAM = {("adamw", "bf16"): 20, ("adamw", "fp32"): 28, ("adamw", "fp8"
                    ("lion", "bf16"): 16, ("lion", "fp32"): 20, ("lion", "fp8"): 14.0625}
 # DRAM bytes (read + write) per parameter of the update kernel, from one ncu capture of the small Llama case
 # (1 layer, vocab 8000: 267,923,456 parameters); the traffic of a launch grows with its parameters, so the
-# full-size figure is this times the parameters a step updates.  Summaries: profiles/update_kernel_adamw_*.md
-# NVLink 5 peer copy measured on this pool's B200s, per direction per GPU (900 GB/s nominal): the denominator for a
-# kernel bound by its stores into the peers' memory
-NVLINK_PEER_GBS = 770.0
+# full-size figure is this times the parameters a step updates.
 MEASURED_DRAM_BYTES_PER_PARAM = {("adamw", "bf16"): (2.679388e9 + 2.622009e9) / 267923456,
                                  ("adamw", "fp8"): (2.160363e9 + 2.111521e9) / 267923456}
 
@@ -115,37 +112,75 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- CPU baseline
 
-def cpu_reference_sample(seconds: float = 10.0, steps: int | None = None, warmup: int = 1):
-    """Time the reference's own kernel library (oracle/_ref) -- or, where it was not built, the oracle port --
-    on one Llama-7B decoder layer's seven matrices (202,375,168 params; bf16 moments, bf16 grad and weights,
-    fp32 master), all host threads.  Returns (Gparams/s, threads, kind, sample description, ms per step)."""
-    import ctypes
+def metric_name(algo: str, prec: str) -> str:
+    """The metric string of a bench line (the same on the repo's arm and the reference arm)."""
+    if (algo, prec) == ("adamw", "bf16"):
+        return "fused step Gparams/s and % of HBM roofline (7B, bf16 moments)"
+    return f"fused step Gparams/s ({algo}, {prec} moments)"
 
+
+def workload_name(dims: dict, algo: str, prec: str, clip: float | None) -> str:
+    name = (f"llama7b-{algo}-{prec}-moments" if dims == LLAMA7B else
+            f"llama-{dims['layers']}L-v{dims['vocab']}-{algo}-{prec}-moments")
+    return name + ("" if clip is None else f"-clip{clip:g}")
+
+
+def default_reference_threads() -> int:
+    """The reference's default pool size: two thirds of the usable cores, at most 32 (adambridge/engine.py:635)."""
+    return max(1, min(32, (2 * len(os.sched_getaffinity(0))) // 3))
+
+
+def cpu_reference_sample(seconds: float = 10.0, steps: int | None = None, warmup: int = 1, algo: str = "adamw",
+                         prec: str = "bf16", threads: int | None = None, simd: str | None = None):
+    """Time the reference's own kernel library (oracle/_ref) -- or, where it was not built, the oracle port --
+    on one Llama-7B decoder layer's seven matrices (202,375,168 params; moments in ``prec``, bf16 grad and
+    weights, fp32 master), on ``threads`` host threads (default: every usable core) at SIMD level ``simd``
+    (default: the best this CPU runs).  Returns (Gparams/s, threads, kind, sample description, ms per step)."""
     import numpy as np
 
     from oracle import oracle as O
 
     ref = O.load_reference()
     kind = "reference" if ref is not None else "port"
-    threads = len(os.sched_getaffinity(0)) if ref is not None else 1
+    if ref is None:
+        threads = 1
+    elif threads is None:
+        threads = len(os.sched_getaffinity(0))
     h, mlp = LLAMA7B["hidden"], LLAMA7B["mlp"]
     shapes = [(h, h)] * 4 + [(mlp, h)] * 3
     if ref is None:
         shapes = [(h, h)]   # the single-threaded port gets a smaller sample
+    mv = {"fp32": O.DT_F32, "bf16": O.DT_BF16, "fp8": O.DT_FP8}[prec]
+    alg = O.LION if algo == "lion" else O.ADAMW
     rng = np.random.default_rng(0)
     segs, keep = [], []
-    group = O.Group(lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, seed=0, stochastic=1)
+    group = (O.Group(lr=1e-5, beta1=0.9, beta2=0.99, eps=0.0, weight_decay=0.1, seed=0, stochastic=1) if alg == O.LION
+             else O.Group(lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, seed=0, stochastic=1))
     for i, shp in enumerate(shapes):
         n = numel(shp)
-        hs = O.HostSegment(n, O.DT_BF16, O.DT_BF16, O.DT_BF16, O.DT_F32, O.ADAMW, index=i)
+        hs = O.HostSegment(n, O.DT_BF16, mv, O.DT_BF16, O.DT_F32, alg, index=i)
+        mlen = hs.moment_len()
+        mdt = {O.DT_F32: np.float32, O.DT_BF16: np.uint16, O.DT_FP8: np.uint8}[mv]
         hs.buffers = {"p": (rng.standard_normal(n, dtype=np.float32) * 0.02),
                       "g": O.bf16_bits(rng.standard_normal(n, dtype=np.float32) * 1e-3),
-                      "m": np.zeros(n, np.uint16), "v": np.zeros(n, np.uint16), "out": np.zeros(n, np.uint16)}
+                      "m": np.zeros(mlen, mdt), "out": np.zeros(n, np.uint16)}
+        if alg == O.ADAMW:
+            hs.buffers["v"] = np.zeros(mlen, mdt)
+        if mv == O.DT_FP8:
+            hs.buffers["m_scale"] = np.ones(hs.nblocks, np.float32)
+            if alg == O.ADAMW:
+                hs.buffers["v_scale"] = np.ones(hs.nblocks, np.float32)
         keep.append(hs)
         segs.append(hs.ctype(group))
     total = sum(s.n for s in segs)
     arr = O.seg_array(segs)
     orc = None if ref is not None else O.load_oracle()
+    level = None
+    if ref is not None:
+        saved_level = ref.simd_level
+        if simd is not None:
+            ref.set_simd_level({v: k for k, v in O.SIMD_NAMES.items()}[simd])
+        level = O.SIMD_NAMES[ref.simd_level]
 
     def one(step):
         for s in segs:
@@ -154,35 +189,70 @@ def cpu_reference_sample(seconds: float = 10.0, steps: int | None = None, warmup
         if rc != 0:
             raise RuntimeError(f"CPU baseline update failed ({rc})")
 
-    step = 0
-    for _ in range(warmup):
-        step += 1
-        one(step)
-    times = []
-    t_end = time.perf_counter() + seconds
-    while (steps is None and time.perf_counter() < t_end) or (steps is not None and len(times) < steps):
-        step += 1
-        t0 = time.perf_counter()
-        one(step)
-        times.append(time.perf_counter() - t0)
+    try:
+        step = 0
+        for _ in range(warmup):
+            step += 1
+            one(step)
+        times = []
+        t_end = time.perf_counter() + seconds
+        while (steps is None and time.perf_counter() < t_end) or (steps is not None and len(times) < steps):
+            step += 1
+            t0 = time.perf_counter()
+            one(step)
+            times.append(time.perf_counter() - t0)
+    finally:
+        if ref is not None:
+            ref.set_simd_level(saved_level)
     med = statistics.median(times)
     del keep
-    desc = (f"{len(shapes)} tensors of one Llama-7B layer ({total:,} params), AdamW bf16 moments, bf16 grad/out, "
-            f"{len(times)} steps, median; simd={O.SIMD_NAMES[ref.simd_level] if ref else 'port'}")
+    desc = (f"{len(shapes)} tensors of one Llama-7B layer ({total:,} params), {algo} {prec} moments, bf16 grad/out, "
+            f"{len(times)} steps, median; simd={level or 'port'}")
     return total / med / 1e9, threads, kind, desc, med * 1e3
 
 
+def cpu_baseline_block(args) -> dict:
+    """The reference's CPU path on this host for the bench line: the headline sample on every usable core, plus
+    the variants a reference user would run -- its default pool (2/3 of the cores, at most 32), the same mode at
+    the forced AVX2 level, and the FP8 mode -- each bounded to a few seconds."""
+    algo, prec = args.algorithm, args.precision
+    gps, threads, kind, desc, _ = cpu_reference_sample(seconds=args.cpu_seconds, algo=algo, prec=prec)
+    block = {"value": round(gps, 4), "unit": "Gparams/s", "cores": threads, "kind": kind, "sample": desc}
+    if kind != "reference" or args.cpu_variant_seconds <= 0:
+        return block
+    variants = []
+    wanted = [dict(threads=default_reference_threads(), algo=algo, prec=prec, simd=None, why="reference default pool"),
+              dict(threads=None, algo=algo, prec=prec, simd="avx2", why="forced avx2")]
+    if prec != "fp8":
+        wanted += [dict(threads=None, algo=algo, prec="fp8", simd=None, why="fp8 moments"),
+                   dict(threads=None, algo=algo, prec="fp8", simd="avx2", why="fp8 moments, forced avx2")]
+    for w in wanted:
+        try:
+            v_gps, v_threads, _, v_desc, _ = cpu_reference_sample(seconds=args.cpu_variant_seconds, algo=w["algo"],
+                                                                 prec=w["prec"], threads=w["threads"], simd=w["simd"])
+        except Exception as exc:  # noqa: BLE001 -- a variant this CPU cannot run (no AVX2) is reported, not fatal
+            variants.append({"variant": w["why"], "error": str(exc)})
+            continue
+        variants.append({"variant": w["why"], "value": round(v_gps, 4), "unit": "Gparams/s", "cores": v_threads,
+                         "sample": v_desc})
+    block["variants"] = variants
+    return block
+
+
 def reference_arm(args, rank: int, world: int) -> None:
-    """--impl reference: the reference's CPU implementation on this host, rank 0 only."""
+    """--impl reference: the reference's CPU implementation on this host, rank 0 only, on the same metric,
+    workload and unit as the repo's arm."""
     if rank != 0:
         return
-    gps, threads, kind, desc, ms = cpu_reference_sample(steps=args.steps, warmup=args.warmup)
-    line = {"impl": "reference", "metric": "fused step Gparams/s (7B, bf16 moments)", "value": round(gps, 4),
+    algo, prec = args.algorithm, args.precision
+    gps, threads, kind, desc, ms = cpu_reference_sample(steps=args.steps, warmup=args.warmup, algo=algo, prec=prec)
+    dims = dict(LLAMA7B)
+    line = {"impl": "reference", "metric": metric_name(algo, prec), "value": round(gps, 4),
             "unit": "Gparams/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "llama7b-adamw-bf16-moments (CPU sample: one decoder layer)",
-                       "parallelism": "host threads"},
+            "config": {"workload": workload_name(dims, algo, prec, None), "parallelism": "host threads",
+                       "sample": "each step updates one Llama-7B decoder layer's matrices; Gparams/s is its rate"},
             "cpu_baseline": {"value": round(gps, 4), "unit": "Gparams/s", "cores": threads, "kind": kind,
                              "sample": desc},
             "e2e": {"value": round(gps, 4), "unit": "Gparams/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -258,7 +328,7 @@ def reference_gpu_arm(args, rank: int) -> None:
 
 # --------------------------------------------------------------------------- training workload (config 5)
 
-def train_arm(args, rank: int, world: int, local_rank: int) -> None:
+def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
     """--workload train: the end-to-end training step of the reference's config 5 (with ``--delay``, its
     delayed-update variant) -- a random-init Llama-7B
     decoder (bf16 weights, activation checkpointing per layer), batch 8 x sequence 512 of uniform token ids per
@@ -377,7 +447,7 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> None:
     ms, upd_ms = t.tolist()
     loss_host = float(loss.detach().float().item())
     if rank != 0:
-        return
+        return None
     tokens_per_step = batch * seq * world
     line = {"metric": "training step tokens/s (Llama-7B decoder, ZeRO-1 AdamW bf16 moments, hooks)",
             "value": round(tokens_per_step / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
@@ -390,12 +460,125 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> None:
                        "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None},
             "update_kernels_ms": round(upd_ms, 3), "loss": round(loss_host, 4),
             "gpu_launches": kern.launch_count() - launches0, "clocks": clocks.summary()}
-    print(json.dumps(line), flush=True)
+    return line
+
+
+# --------------------------------------------------------------------------- multi-GPU checks
+
+def sharded_parity(args, world: int, rank: int, dev) -> dict:
+    """After the timed region: is the sharded step the unsharded one, bit for bit, on this node?
+
+    A sample of the 7B set's tensors -- the embedding and the lm_head (each split over ranks), a 4096^2 and
+    both MLP shapes, two norms -- gets two optimizer steps from a ZeroAdamBridge / ZeroLionBridge of this
+    world (the bench's gather mode and precision; gradients handed in as each rank's shard) and from a
+    world-1 AdamBridge / LionBridge on a copy of the same tensors (the same gradients, whole).  Every rank
+    then compares the weights it holds after the all-gather (every element of every sampled tensor, so
+    every peer's stores into this rank are checked) and its own shard of the master and the moments with the
+    unsharded optimizer's.  Mismatch counts are summed over the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from adambridge_b200 import AdamBridge, LionBridge
+    from adambridge_b200.zero import ZeroAdamBridge, ZeroLionBridge
+
+    h, mlp, vocab = LLAMA7B["hidden"], LLAMA7B["mlp"], LLAMA7B["vocab"]
+    shapes = [(vocab, h), (h, h), (h,), (mlp, h), (h, mlp), (h,), (vocab, h)]
+    algo, prec = args.algorithm, args.precision
+    kw = dict(lr=1e-5, betas=(0.9, 0.99), weight_decay=0.1) if algo == "lion" else \
+        dict(lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    gen = torch.Generator(device=dev).manual_seed(4321)      # the same tensors on every rank
+    with torch.no_grad():
+        init = [torch.empty(s, dtype=torch.bfloat16, device=dev).normal_(0.0, 0.02, generator=gen) for s in shapes]
+    zparams = [torch.nn.Parameter(w.clone()) for w in init]
+    aparams = [torch.nn.Parameter(w.clone()) for w in init]
+    del init
+    zcls, acls = (ZeroLionBridge, LionBridge) if algo == "lion" else (ZeroAdamBridge, AdamBridge)
+    zopt = zcls(zparams, precision=prec, gather=args.gather, max_ctas=args.max_ctas, **kw)
+    aopt = acls(aparams, precision=prec, **kw)
+    L = zopt.layout
+    pieces = [pc for rnd in zopt._pieces for pc in rnd]
+    for step in range(2):
+        gen = torch.Generator(device=dev).manual_seed(9000 + step)
+        with torch.no_grad():
+            grads = [torch.empty(s, dtype=torch.bfloat16, device=dev).normal_(0.0, 1e-3, generator=gen)
+                     for s in shapes]
+            for pc in pieces:
+                zopt.grad_shard[pc.local_lo:pc.local_lo + pc.n].copy_(grads[pc.index].view(-1)[pc.t_lo:pc.t_hi])
+        zopt.step_shard()
+        for p, g in zip(aparams, grads):
+            p.grad = g
+        aopt.step()
+        aopt.zero_grad(set_to_none=True)
+    torch.cuda.synchronize(dev)
+
+    def bits(t):
+        return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
+
+    checked = torch.zeros(2, dtype=torch.int64, device=dev)    # (elements compared, mismatches)
+    with torch.no_grad():
+        for zp, ap in zip(zparams, aparams):
+            checked[0] += zp.numel()
+            checked[1] += (bits(zp.detach()) != bits(ap.detach())).sum()
+        zstores = [("master", zopt.master), ("m", zopt.m)] + ([] if zopt.v is None else [("v", zopt.v)])
+        for pc in pieces:
+            slot = aopt._ordered[pc.index]
+            for name, zst in zstores:
+                ast = getattr(slot, name)
+                zbuf, zsc = zst.native_buffers
+                abuf, asc = ast.native_buffers
+                for a, b in ((zbuf[pc.local_lo:pc.local_lo + pc.n], abuf[pc.t_lo:pc.t_hi]),
+                             (zsc[pc.local_lo // 128:-(-(pc.local_lo + pc.n) // 128)] if zsc is not None else None,
+                              asc[pc.t_lo // 128:-(-pc.t_hi // 128)] if asc is not None else None)):
+                    if a is None:
+                        continue
+                    checked[0] += a.numel()
+                    checked[1] += (bits(a) != bits(b)).sum()
+    if world > 1:
+        dist.all_reduce(checked)
+    straddling = sum(1 for i in range(len(shapes))
+                     if len({r for r in range(world) for rnd in L.pieces(r) for pc in rnd if pc.index == i}) > 1)
+    n_checked, n_bad = (int(x) for x in checked.tolist())
+    del zopt, aopt, zparams, aparams
+    torch.cuda.empty_cache()
+    return {"checked": n_checked, "mismatches": n_bad, "tensors": len(shapes), "split_over_ranks": straddling,
+            "steps": 2, "against": f"world-1 {acls.__name__} on the same tensors and gradients",
+            "gather": "fused peer stores" if world > 1 and args.gather != "nccl" else ("nccl" if world > 1 else None)}
+
+
+def nccl_allgather_gbs(opt, world: int, dev, iters: int = 5) -> float:
+    """NVLink ingress per rank (GB/s) that NCCL's in-place all-gather reaches on the step's own weight buffer
+    (every rank receives (world - 1) x its shard): the reference rate for the fused all-gather."""
+    import torch
+    import torch.distributed as dist
+
+    L = opt.layout
+    buf = opt.flat_weights
+    mine = [buf[slice(*L.rank_range(r, opt.rank))] for r in range(L.rounds)]
+    outs = [buf[slice(*L.round_range(r))] for r in range(L.rounds)]
+    cur = torch.cuda.current_stream(dev)
+
+    def once():
+        for out, m in zip(outs, mine):
+            dist.all_gather_into_tensor(out, m)
+
+    once()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(cur)
+    for _ in range(iters):
+        once()
+    b.record(cur)
+    torch.cuda.synchronize(dev)
+    ms = torch.tensor([a.elapsed_time(b) / iters], dtype=torch.float64, device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    received = (world - 1) * L.chunk * L.rounds * buf.element_size()
+    return received / (ms.item() / 1e3) / 1e9
 
 
 # --------------------------------------------------------------------------- GPU arm
 
-def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
+def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     import torch.distributed as dist
 
@@ -507,15 +690,21 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                        f"round by round ({L.rounds} rounds) overlapping the updates"}
         del host_g, host_w
 
+    # ---- N > 1: the NVLink reference rate (NCCL's all-gather of the same bytes), then the parity check
+    nccl_gbs = nccl_allgather_gbs(opt, world, dev) if world > 1 else None
+    fused_gather = world > 1 and opt._peer_deltas is not None
+    del opt
+    torch.cuda.empty_cache()
+    parity = None if args.no_parity else sharded_parity(args, world, rank, dev)
+
     if rank != 0:
-        return
+        return None
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
         peaks = json.loads(pk.read_text())
     peak = peaks.get("hbm_gbs", 6650.0)
     peak_note = "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks else "6650 GB/s (of fallback)"
-    fused_gather = world > 1 and opt._peer_deltas is not None
     hbm_bytes = bpp * shard_params
     nvl_bytes = 0
     if fused_gather:
@@ -523,24 +712,22 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         # peers' (NVLink ingress, written into this GPU's HBM): per direction, (world - 1) x its shard
         nvl_bytes = (world - 1) * shard_params * 2
         hbm_bytes += nvl_bytes
-    bound = "nvlink" if nvl_bytes / NVLINK_PEER_GBS > hbm_bytes / peak else "hbm"
+    bound = "nvlink" if fused_gather and nvl_bytes / nccl_gbs > hbm_bytes / peak else "hbm"
     if bound == "nvlink":
         achieved = nvl_bytes / (kernel_ms_max / 1e3) / 1e9
-        peak, peak_note = NVLINK_PEER_GBS, f"{NVLINK_PEER_GBS:.0f} GB/s peer copy per direction (of measured on this pool)"
+        peak, peak_note = round(nccl_gbs, 1), (f"{nccl_gbs:.0f} GB/s NVLink ingress per rank of NCCL's all-gather of "
+                                               "the same weight buffer, measured in this run (of measured)")
     else:
         achieved = hbm_bytes / (kernel_ms_max / 1e3) / 1e9
     line = {
-        "metric": "fused step Gparams/s and % of HBM roofline (7B, bf16 moments)" if (algo, prec) == ("adamw", "bf16")
-        else f"fused step Gparams/s ({algo}, {prec} moments)",
+        "metric": metric_name(algo, prec),
         "value": round(n_params / (ms_max / 1e3) / 1e9, 4), "unit": "Gparams/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": (f"llama7b-{algo}-{prec}-moments" if dims == LLAMA7B else
-                                f"llama-{dims['layers']}L-v{dims['vocab']}-{algo}-{prec}-moments")
-                   + ("" if args.clip is None else f"-clip{args.clip:g}"), "params": n_params, "tensors": len(shapes),
+        "config": {"workload": workload_name(dims, algo, prec, args.clip), "params": n_params, "tensors": len(shapes),
                    "weights": "bf16", "grads": "bf16", "master": "fp32", "stochastic_rounding": True,
                    "parallelism": f"zero1-dp{world}", "rounds": L.rounds, "max_ctas": args.max_ctas,
-                   "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None,
+                   "all_gather": ("fused peer stores" if fused_gather else "nccl") if world > 1 else None,
                    "l2": "no flush: each step streams %.1f GB >> 126 MB L2" % (bpp * shard_params / 1e9)},
         "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
@@ -564,13 +751,17 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                         "basis": "clip_shard_grad_norm_ before every step: one read of the bf16 gradient shard "
                                  "(per-tensor sums of squares), the coefficient applied inside the update kernel"}
     if world > 1:
-        line["allgather"] = {"bytes_received_per_rank": int((world - 1) * L.chunk * L.rounds * 2),
-                             "step_ms": round(ms_max, 3), "update_kernel_ms": round(kernel_ms_max, 3)}
+        received = (world - 1) * L.chunk * L.rounds * 2
+        line["allgather"] = {"bytes_received_per_rank": int(received), "step_ms": round(ms_max, 3),
+                             "update_kernel_ms": round(kernel_ms_max, 3),
+                             "nccl_allgather_gbs": round(nccl_gbs, 1),
+                             "limited_by": ("NVLink ingress of the update kernel's peer stores" if bound == "nvlink"
+                                            else "HBM traffic of the update kernel")}
+    if parity is not None:
+        line["parity"] = parity
     if world == 1 and not args.no_cpu_baseline:
-        gps, threads, kind, desc, _ = cpu_reference_sample(seconds=args.cpu_seconds)
-        line["cpu_baseline"] = {"value": round(gps, 4), "unit": "Gparams/s", "cores": threads, "kind": kind,
-                                "sample": desc}
-    print(json.dumps(line), flush=True)
+        line["cpu_baseline"] = cpu_baseline_block(args)
+    return line
 
 
 def main() -> int:
@@ -596,8 +787,11 @@ def main() -> int:
                     help="--workload train: delayed updates (each update overlaps the next forward)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-variant-seconds", type=float, default=3.0,
+                    help="seconds per extra CPU-baseline variant (default pool, forced avx2, fp8); 0 skips them")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the sharded-vs-unsharded check after timing")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "abx":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -615,20 +809,34 @@ def main() -> int:
 
     import torch
     import torch.distributed as dist
+    result_fd = None
     if world > 1:
-        # NCCL's own banner would precede the result line on stdout
-        os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL logs its communicators (INFO: ranks, devices, transports) to standard output.  Everything this
+        # process writes to standard output from here on goes to standard error instead, so the result line,
+        # written to the saved descriptor, is the only line on standard output.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        sys.stdout.flush()
+        result_fd = os.dup(1)
+        os.dup2(2, 1)
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+    line = None
     try:
         if args.workload == "train":
-            train_arm(args, rank, world, local_rank)
+            line = train_arm(args, rank, world, local_rank)
         else:
-            gpu_arm(args, rank, world, local_rank)
+            line = gpu_arm(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()
+    if line is not None:
+        text = json.dumps(line) + "\n"
+        if result_fd is None:
+            sys.stdout.write(text)
+            sys.stdout.flush()
+        else:
+            os.write(result_fd, text.encode())
     return 0
 
 

@@ -227,7 +227,9 @@ int abx_clip_coef(void* stream, const abx_tensor* grads, int32_t n, float max_no
  *   524,288 (about 8.59e9 elements); more is rejected before anything runs, with ABX_E_SCRATCH
  *   and a message in abx_last_error().
  *   Set-up: the first call on each device looks up the array's address (cudaGetSymbolAddress,
- *   with that device current); make that first call before any stream capture.
+ *   with that device current); make that first call before any stream capture.  The address
+ *   belongs to a CUDA context: a call under another context than the one it was looked up in
+ *   (after cudaDeviceReset, or a non-primary context) looks it up again, as a first call does.
  *   Nothing needs to start at zero: every partial a call reads was written earlier in that call.
  *   All calls on one device share the array: calls whose work overlaps on the device (two
  *   streams, or two host threads without ordering between them) race on it. */

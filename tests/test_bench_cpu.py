@@ -11,6 +11,8 @@ import sys
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
 
 
 def test_reference_arm_prints_one_contract_line():
@@ -27,6 +29,36 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference" and d["value"] > 0 and d["steps"] == 2
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
+    # the driver divides the two arms' values only when metric, unit and direction agree
+    import bench
+    assert d["metric"] == bench.metric_name("adamw", "bf16")
+    assert d["config"]["workload"] == bench.workload_name(bench.LLAMA7B, "adamw", "bf16", None)
+    assert d["unit"] == "Gparams/s" and d["higher_is_better"] is True
+
+
+def test_reference_arm_other_modes():
+    env = dict(os.environ, WORLD_SIZE="1", RANK="0", LOCAL_RANK="0")
+    p = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1",
+                        "--algorithm", "lion", "--precision", "fp8"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=600, env=env)
+    assert p.returncode == 0, p.stderr[-2000:]
+    d = json.loads(p.stdout.strip().splitlines()[-1])
+    import bench
+    assert d["metric"] == bench.metric_name("lion", "fp8") and d["value"] > 0
+    assert "lion fp8 moments" in d["cpu_baseline"]["sample"]
+
+
+def test_cpu_baseline_variants():
+    import argparse
+
+    import bench
+    args = argparse.Namespace(algorithm="adamw", precision="bf16", cpu_seconds=0.5, cpu_variant_seconds=0.2)
+    block = bench.cpu_baseline_block(args)
+    assert block["value"] > 0 and block["cores"] >= 1
+    if block["kind"] == "reference":
+        names = [v["variant"] for v in block["variants"]]
+        assert names == ["reference default pool", "forced avx2", "fp8 moments", "fp8 moments, forced avx2"]
+        assert block["variants"][0]["cores"] == bench.default_reference_threads()
 
 
 def test_reference_arm_other_ranks_print_nothing():
@@ -40,5 +72,5 @@ def test_flags_parse():
     p = subprocess.run([sys.executable, "bench.py", "--help"], cwd=ROOT, capture_output=True, text=True, timeout=120)
     assert p.returncode == 0
     for flag in ("--gpus", "--steps", "--warmup", "--impl", "--workload", "--algorithm", "--precision", "--rounds",
-                 "--gather", "--clip", "--no-e2e", "--no-cpu-baseline"):
+                 "--gather", "--clip", "--no-e2e", "--no-cpu-baseline", "--no-parity", "--cpu-variant-seconds"):
         assert flag in p.stdout, flag
