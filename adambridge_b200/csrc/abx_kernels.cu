@@ -22,8 +22,9 @@
 //     global store of a warp covers one contiguous span without bank conflicts.
 //     With FP8 moments one 128-element block is exactly one warp's group; the
 //     block maxima for the new scales are reduced with xor-shuffles.
-//   * Every mbarrier wait is bounded: a wait that gives up sets a device status
-//     word (read by abx_pipeline_status) and the CTA drains its copies and exits.
+//   * Every mbarrier wait is bounded: a wait that gives up sets a status word in
+//     mapped host memory (abx_status_word / abx_pipeline_status, readable by the
+//     host without a device synchronization) and the CTA drains its copies and exits.
 //
 // Bit-exactness with the reference (adambridge/csrc/adambridge_kernels.c) is
 // obtained by restating every operation with an explicit rounding intrinsic and
@@ -53,11 +54,14 @@ constexpr int kTile = 2 * kHalf;                       // 2048 elements per tile
 constexpr int kMaxSegs = 64;                           // segments per launch (parameter block ~10 KB)
 constexpr int kMinCtasPerSm = 4;                       // residency the register budget is set for (<= 56 regs)
 constexpr int kSmemTarget = 52 * 1024;                 // ring bytes per CTA (four CTAs per SM)
-constexpr uint32_t kSpinLimit = 1u << 22;              // mbarrier polls before a wait gives up
+constexpr uint32_t kSpinLimit = 1u << 22;              // mbarrier polls before a wait gives up (default)
 constexpr int kMaxReplicas = 7;                        // out replicas per segment (peers of an 8-GPU node)
 
-// Set (OR) by a CTA whose pipeline wait gave up; never set in correct operation.
-__device__ unsigned int g_pipeline_status;
+// Bits of the status word a CTA sets (OR) when one of its pipeline waits gives up; never set in correct
+// operation.  The word lives in mapped, pinned host memory, so the host reads it without synchronizing.
+constexpr unsigned int kStatusConsumerWait = 1u;   // a consumer warp's wait for a staged tile
+constexpr unsigned int kStatusProducerWait = 2u;   // the producer's wait for a free ring slot
+constexpr unsigned int kStatusDrainWait = 4u;      // the producer's wait for its last copies before it exits
 
 // Device copy of one segment with its per-step coefficients.
 struct KSeg {
@@ -90,6 +94,11 @@ struct KArgs {
     int32_t stages;
     int64_t total_tiles;
     const float* g_scale;     // optional device scalar multiplying every gradient element
+    unsigned int* status;     // the status word (mapped host memory)
+    uint32_t spin_limit;      // mbarrier polls before a wait gives up
+    int32_t pad0;
+    int64_t skip_tile;        // failure-path test only (abx_test_pipeline_fault): the producer leaves this tile's
+                              // stage untouched -- no copy, no arrival -- so its consumers' wait runs out; else -1
     KSeg seg[NSEG];
 };
 
@@ -158,12 +167,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
-// Wait for the phase of `bar` with parity `parity`; false (and the status word set) if it never completes.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
+// Wait for the phase of `bar` with parity `parity`, at most `limit` polls; false (and `what` set in the
+// status word) if it never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit, unsigned int* status,
+                                          unsigned int what)
 {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
+    for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
-    atomicOr(&g_pipeline_status, 1u);
+    atomicOr_system(status, what);
     return false;
 }
 
@@ -944,7 +955,11 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
         int k = 0, s = 0;
         uint32_t ph = 0;   // parity of the current pass over the ring (s and ph track k % S and (k / S) & 1)
         for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x, ++k) {
-            if (!mbar_wait(&empty[s], ph ^ 1)) break;
+            if (!mbar_wait(&empty[s], ph ^ 1, a.spin_limit, a.status, kStatusProducerWait)) break;
+            if (t == a.skip_tile) {   // failure-path test: nothing is copied into, or arrives on, this stage
+                if (++s == S) { s = 0; ph ^= 1; }
+                continue;
+            }
             const int si = find_segment(a, t);
             const KSeg& Sg = a.seg[si];
             const int64_t base = (t - Sg.tile_begin) * kTile;
@@ -978,8 +993,10 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
             }
             if (++s == S) { s = 0; ph ^= 1; }
         }
-        // never leave with bulk copies in flight into this CTA's shared memory
-        for (int j = k - S < 0 ? 0 : k - S; j < k; ++j) mbar_wait(&full[j % S], (j / S) & 1);
+        // never leave with bulk copies in flight into this CTA's shared memory (the stage of a skipped tile
+        // had none, and its wait gives up like the others)
+        for (int j = k - S < 0 ? 0 : k - S; j < k; ++j)
+            mbar_wait(&full[j % S], (j / S) & 1, a.spin_limit, a.status, kStatusDrainWait);
         return;
     }
 
@@ -988,7 +1005,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) update_kernel(const _
     int s = 0;
     uint32_t ph = 0;
     for (int64_t t = blockIdx.x; t < a.total_tiles; t += gridDim.x) {
-        if (!mbar_wait(&full[s], ph)) return;
+        if (!mbar_wait(&full[s], ph, a.spin_limit, a.status, kStatusConsumerWait)) return;
         const TileMeta tm = hdr[s].meta;
         const KSeg& Sg = hdr[s].seg;
         if (tm.staged) {
@@ -1015,10 +1032,35 @@ thread_local char g_err[512] = "";
 std::atomic<int> g_simd_level{ABX_SIMD_AVX512};
 std::atomic<uint64_t> g_launches{0};
 
+// The pipeline status word: one unsigned int in pinned host memory mapped into every device's address
+// space (portable), allocated at the first launch.  Kernels OR failure bits into it with system-scope
+// atomics; the host reads it with no CUDA call.
+std::once_flag g_status_once;
+unsigned int* g_status = nullptr;
+cudaError_t g_status_err = cudaSuccess;
+
+// Failure-path test settings (abx_test_pipeline_fault), copied into the next launches' arguments.
+std::atomic<int64_t> g_skip_tile{-1};
+std::atomic<uint32_t> g_spin_limit{kSpinLimit};
+
 int set_error(const char* what, cudaError_t e)
 {
     snprintf(g_err, sizeof g_err, "%s: %s", what, cudaGetErrorString(e));
     return ABX_E_CUDA;
+}
+
+unsigned int* status_word(int* rc)
+{
+    std::call_once(g_status_once, [] {
+        void* p = nullptr;
+        g_status_err = cudaHostAlloc(&p, 64, cudaHostAllocMapped | cudaHostAllocPortable);
+        if (g_status_err == cudaSuccess) {
+            g_status = static_cast<unsigned int*>(p);
+            *reinterpret_cast<volatile unsigned int*>(g_status) = 0;
+        }
+    });
+    if (!g_status) *rc = set_error("allocating the pipeline status word", g_status_err);
+    return g_status;
 }
 
 int lanes_of(int level)
@@ -1250,6 +1292,10 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
     int rc = ABX_OK;
     DeviceInfo* dev = device_info(&rc);
     if (!dev) return rc;
+    unsigned int* status = status_word(&rc);
+    if (!status) return rc;
+    const uint32_t spin_limit = g_spin_limit.load();
+    int64_t skip_tile = g_skip_tile.exchange(-1);   // a test's fault applies to the next launch only
     const int lanes = lanes_of(g_simd_level.load());
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 
@@ -1272,6 +1318,10 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
                 a.stages = stages_of(kind);
                 a.total_tiles = tiles_of(segs[i]->n);
                 a.g_scale = g_scale;
+                a.status = status;
+                a.spin_limit = spin_limit;
+                a.skip_tile = skip_tile;
+                skip_tile = -1;
                 e = kLaunchOne[kind](a, grid_for(a.total_tiles, dev->blocks_one[kind], dev->sms, max_ctas), smem, st);
             } else {
                 static thread_local KArgs<kMaxSegs> a;   // ~10 KB: kept off the stack
@@ -1286,6 +1336,10 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
                 a.stages = stages_of(kind);
                 a.total_tiles = tiles;
                 a.g_scale = g_scale;
+                a.status = status;
+                a.spin_limit = spin_limit;
+                a.skip_tile = skip_tile;
+                skip_tile = -1;
                 e = kLaunchMany[kind](a, grid_for(tiles, dev->blocks_many[kind], dev->sms, max_ctas), smem, st);
             }
             if (e != cudaSuccess) return set_error("kernel launch", e);
@@ -1422,13 +1476,33 @@ ABX_API uint64_t abx_launch_count(void) { return abx::g_launches.load(); }
 
 ABX_API const char* abx_last_error(void) { return abx::g_err; }
 
-// Nonzero when a kernel's pipeline wait gave up since the last call (then reset).  Synchronizes the
-// current device; a correct pipeline never sets it.
+// The status word's bits (nonzero: an update kernel's pipeline wait gave up, so some update since the
+// last call is incomplete), then cleared.  No device synchronization: it covers the kernels that have
+// finished when it is called.
 ABX_API int abx_pipeline_status(void)
 {
-    unsigned int v = 0, zero = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&v, abx::g_pipeline_status, sizeof v);
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(abx::g_pipeline_status, &zero, sizeof zero);
-    if (e != cudaSuccess) return abx::set_error("reading the pipeline status", e);
-    return (int)v;
+    int rc = ABX_OK;
+    unsigned int* w = abx::status_word(&rc);
+    if (!w) return rc;
+    return (int)__atomic_exchange_n(w, 0u, __ATOMIC_SEQ_CST);
+}
+
+// Host address of the status word (mapped pinned memory; NULL if it cannot be allocated): a caller may
+// poll it directly, without any CUDA call.
+ABX_API const volatile unsigned int* abx_status_word(void)
+{
+    int rc = ABX_OK;
+    return abx::status_word(&rc);
+}
+
+// Failure-path testing only: the next launch's producer skips element tile `tile` of its tile space (no bulk
+// copy is issued into that ring stage and nothing arrives on its barrier), and from now on every mbarrier
+// wait gives up after `spin_limit` polls (0 restores the default).  The consumers waiting for the skipped
+// tile give up, the status word is set, and the CTA's later tiles stay unupdated -- the effect of a pipeline
+// fault, made without a fault.  tile < 0 cancels a pending skip.
+ABX_API int abx_test_pipeline_fault(int64_t tile, uint32_t spin_limit)
+{
+    abx::g_spin_limit.store(spin_limit == 0 ? abx::kSpinLimit : spin_limit);
+    abx::g_skip_tile.store(tile < 0 ? -1 : tile);
+    return ABX_OK;
 }

@@ -376,9 +376,12 @@ class UpdateEngine:
     # ------------------------------------------------------------------ synchronizing
 
     def wait(self) -> None:
-        """Block until every enqueued update has finished on the GPU."""
+        """Block until every enqueued update has finished on the GPU; raise if one of them gave up a pipeline
+        wait (its parameters were left partly updated)."""
         for stream in list(self._streams.values()):
             stream.synchronize()
+        if self._streams:
+            self.native.check_status("UpdateEngine.wait")
 
     def _order_writebacks(self) -> None:
         """The caller's current streams wait for the updates (or, delayed, for the write-back copies)."""
@@ -408,7 +411,10 @@ class UpdateEngine:
 
     def flush(self) -> None:
         """Apply every pending (delayed or deferred) update to the parameters; the caller's current stream then
-        sees the weights an exact, undelayed optimizer would have produced."""
+        sees the weights an exact, undelayed optimizer would have produced.  Raises if an update that has
+        finished gave up a pipeline wait."""
+        if self._streams:
+            self.native.check_status("flush")
         with self._lock:
             slots = list({**self._owed, **self._fresh, **self._unwritten})
             self._owed, self._fresh, self._unwritten = {}, {}, {}
@@ -426,7 +432,12 @@ class UpdateEngine:
         """Order this step's updates before the caller's next GPU work.
 
         Delayed mode: only the write-back copies are waited for; updates from earlier steps whose parameters got
-        no gradient this step are written back now, so no parameter lags by more than one step."""
+        no gradient this step are written back now, so no parameter lags by more than one step.
+
+        Raises if an update kernel that has finished by now gave up a pipeline wait (a status word in mapped
+        host memory, read without synchronizing: a failure surfaces at the first step_sync after its kernel)."""
+        if self._streams:
+            self.native.check_status("step_sync")
         t0 = time.perf_counter()
         if self.delay:
             with self._lock:

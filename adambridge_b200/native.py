@@ -217,6 +217,9 @@ class NativeKernels:
         lib.abx_last_error.restype = ctypes.c_char_p
         lib.abx_launch_count.restype = ctypes.c_uint64
         lib.abx_pipeline_status.restype = ctypes.c_int
+        lib.abx_status_word.restype = ctypes.POINTER(ctypes.c_uint)
+        lib.abx_test_pipeline_fault.restype = ctypes.c_int
+        lib.abx_test_pipeline_fault.argtypes = [ctypes.c_int64, ctypes.c_uint32]
         tens = ctypes.POINTER(Tensor)
         lib.abx_clip_workspace_bytes.restype = ctypes.c_size_t
         lib.abx_clip_workspace_bytes.argtypes = [tens, ctypes.c_int32]
@@ -359,12 +362,31 @@ class NativeKernels:
         self._check(rc, "abx_clip_coef_noalloc")
 
     def pipeline_status(self) -> int:
-        """Nonzero if an update kernel's bounded pipeline wait gave up since the last call (then cleared).
-        Synchronizes with the current device."""
+        """The status word's bits -- nonzero if an update kernel's bounded pipeline wait gave up since the last
+        call (1: a consumer's wait for a tile, 2: the producer's wait for a free stage, 4: its wait for its last
+        copies) -- then cleared.  No synchronization: it covers the kernels that have finished."""
         rc = self._lib.abx_pipeline_status()
         if rc < 0:
             self._check(rc, "abx_pipeline_status")
         return rc
+
+    def status_pending(self) -> bool:
+        """Whether the status word is set, read from mapped host memory without clearing it or any CUDA call."""
+        w = self._lib.abx_status_word()
+        return bool(w) and w[0] != 0
+
+    def check_status(self, where: str) -> None:
+        """Raise if an update kernel that has finished gave up a pipeline wait: its tensors were left partly
+        updated.  Clears the word."""
+        if self.status_pending():
+            bits = self.pipeline_status()
+            raise RuntimeError(f"{where}: an update kernel's pipeline wait gave up (status {bits:#x}); the "
+                               "optimizer state of this step is incomplete and should be restored from a checkpoint")
+
+    def test_pipeline_fault(self, tile: int, spin_limit: int = 0) -> None:
+        """Failure-path tests only: the next launch skips tile ``tile`` (no copy, no arrival), and every wait
+        gives up after ``spin_limit`` polls from now on (0: the default).  See abx_test_pipeline_fault."""
+        self._lib.abx_test_pipeline_fault(int(tile), int(spin_limit))
 
     @staticmethod
     def make_hparams(c: StepCoefficients, seed: int, stochastic: bool) -> _HParams:

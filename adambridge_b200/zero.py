@@ -358,7 +358,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     @torch.no_grad()
     def flush(self) -> None:
-        """Apply a pending delayed update to the parameters (before evaluating or saving)."""
+        """Apply a pending delayed update to the parameters (before evaluating or saving).  Raises if an update
+        kernel that has finished gave up a pipeline wait."""
+        self.kernels.check_status("flush")
         self._apply_pending(torch.cuda.current_stream(self.device))
 
     def _refresh(self) -> None:
@@ -635,6 +637,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     def _run(self, flat_grads: torch.Tensor | None, g_scale: torch.Tensor | None = None,
              synced: bool = False, host_in: torch.Tensor | None = None, host_out: torch.Tensor | None = None) -> None:
+        # an update kernel of an earlier step that gave up a pipeline wait left its shard partly updated
+        # (a status word in mapped host memory, read without synchronizing)
+        self.kernels.check_status("ZeroAdamBridge.step")
         L = self.layout
         cur = torch.cuda.current_stream(self.device)
         had_pending = self._delay_owed

@@ -241,10 +241,27 @@ uint64_t abx_launch_count(void);
 
 /* The update kernels stream tiles through shared memory behind mbarrier waits,
  * each bounded: a wait that gives up (never in correct operation) makes its CTA
- * drain its copies and exit, and sets a status word on the device.  Returns that
- * word for the current device (nonzero: some update since the last call is
- * incomplete) and clears it, or ABX_E_CUDA.  Synchronizes with the device. */
+ * drain its copies and exit, and ORs a bit into a status word held in pinned host
+ * memory mapped into every device (1: a consumer's wait for a tile, 2: the
+ * producer's wait for a free stage, 4: the producer's wait for its last copies).
+ * No counterpart in the reference (its host kernels do not wait).
+ * abx_pipeline_status returns the word and clears it (nonzero: some update since
+ * the last call is incomplete), or ABX_E_CUDA if the word cannot be allocated.  It
+ * does not synchronize: it covers the kernels that have finished by then. */
 int abx_pipeline_status(void);
+
+/* Host address of the status word, for callers that poll it without any CUDA
+ * call (NULL if it cannot be allocated).  No counterpart in the reference. */
+const volatile unsigned int* abx_status_word(void);
+
+/* Failure-path testing only; no counterpart in the reference.  The next launch's
+ * producer leaves tile `tile` of its tile space (2048-element tiles of all its
+ * segments, in order) untouched -- no copy into its ring stage, no arrival on its
+ * barrier -- and from now on every wait gives up after `spin_limit` polls (0: the
+ * default, 2^22).  The consumers of that tile give up, the status word is set and
+ * the rest of that CTA's tiles are left unupdated: the effect of a pipeline fault
+ * without one.  tile < 0 cancels a pending skip.  Returns ABX_OK. */
+int abx_test_pipeline_fault(int64_t tile, uint32_t spin_limit);
 
 /* Message of the last ABX_E_CUDA / ABX_E_ALIGN / ABX_E_SCRATCH error on this thread (never NULL). */
 const char* abx_last_error(void);
