@@ -26,7 +26,7 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIBDIR = PKG / "_lib"
 LIB = LIBDIR / "libabx.so"
-SOURCES = [CSRC / "abx_kernels.cu", CSRC / "abx_clip.cu"]
+SOURCES = [CSRC / "abx_kernels.cu", CSRC / "abx_clip.cu", CSRC / "abx_convert.cu"]
 DEPENDS = SOURCES + [CSRC / "abx_device.cuh", INCLUDE / "abx.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -236,6 +236,35 @@ int abx_clip_coef(void* stream, const abx_tensor* grads, int32_t n, float max_no
 int abx_clip_coef_noalloc(void* stream, const abx_tensor* grads, int32_t n, float max_norm, float* sq, float* norms,
                           float* total_coef);
 
+/* One optimizer-state buffer for abx_convert: n values stored in one of the state
+ * formats.  No counterpart struct in the reference, whose stores are torch tensors
+ * (adambridge/precision.py:286-480); the planes and their meaning are its formats. */
+typedef struct abx_state {
+    void* values;     /* ABX_DT_F32: float[n]; ABX_DT_BF16: bf16 bits uint16[n];
+                         ABX_DT_FP8: codes uint8[nblocks * block] (padded to whole blocks);
+                         ABX_DT_F24: the hi plane, bf16 bits uint16[n] */
+    void* aux;        /* ABX_DT_FP8: float scale[nblocks]; ABX_DT_F24: the lo plane uint8[n]; else NULL */
+    int32_t dtype;    /* ABX_DT_F32, ABX_DT_BF16, ABX_DT_FP8 or ABX_DT_F24 */
+    int32_t role;     /* ABX_DT_FP8 only: 0 = first moment (E4M3 codes of m),
+                         1 = second moment (E5M2 codes of sqrt(v)) */
+    int64_t block;    /* ABX_DT_FP8 only: values per scale; a destination must use ABX_FP8_BLOCK,
+                         a source any block in [1, 2^20] */
+} abx_state;
+
+/* Convert n values from src to dst (distinct buffers) on `stream`: each value is decoded
+ * to fp32 and re-encoded in dst's format with round-to-nearest-even, as the reference's
+ * own conversions round (adambridge/precision.py: BF16Store.write :319-323 and torch's
+ * bfloat16 cast, FP8Store.read/write :374-398 without a seed -- a second moment kept as
+ * sqrt(max(v, 0)), scale = block absmax / 448 or / 57344 (1 for an all-zero or NaN
+ * block), values divided, clamped to the format's range and cast --, FP24Store.read/
+ * write :448-462).  NaN becomes 0x7fc0 in bf16 and code 0x7f (with its sign) in FP8, as
+ * torch's casts give them.  An FP8 destination's padding codes (up to the block end) are
+ * written as 0.  No counterpart entry point in the reference (it converts with torch on
+ * the host).  Errors before launch: ABX_E_ARG (n < 0, a bad role or block),
+ * ABX_E_MV_DTYPE, ABX_E_NULL_PTR, ABX_E_SCALE_NULL (FP8 scales or the fp24 lo plane
+ * missing), ABX_E_ALIGN; ABX_E_CUDA on a launch failure. */
+int abx_convert(void* stream, const abx_state* src, const abx_state* dst, int64_t n);
+
 /* Kernel launches this library has made in this process, all threads and devices. */
 uint64_t abx_launch_count(void);
 

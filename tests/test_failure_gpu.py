@@ -70,7 +70,7 @@ def test_adambridge_raises_and_leaves_the_skipped_tile(fault):
 def test_status_word_is_readable_without_synchronizing(fault):
     n = 8 * TILE
     p = torch.nn.Parameter(torch.randn(n, device="cuda", dtype=torch.bfloat16))
-    opt = ab.AdamBridge([p], lr=1e-2, precision="fp32")
+    opt = ab.AdamBridge([p], lr=1e-2, precision="fp32", small_param_threshold=0)   # updated on its own
     p.grad = torch.randn_like(p)
     opt.step()
     torch.cuda.synchronize()
