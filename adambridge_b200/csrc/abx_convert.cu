@@ -55,7 +55,7 @@ struct ConvArgs {
 
 // ---- decoding ------------------------------------------------------------------------------
 
-// FP8 code -> float, exact (finite codes; E4M3 0x7f/0xff are NaN, E5M2 infinities and NaNs keep their meaning).
+// FP8 code -> float, exact for every finite code and the infinities (E5M2 0x7c/0xfc).
 __device__ __forceinline__ float fp8_value(uint32_t code, bool e5m2)
 {
     const uint16_t c2 = (uint16_t)(code & 0xffU);
@@ -67,6 +67,16 @@ __device__ __forceinline__ float fp8_value(uint32_t code, bool e5m2)
     float x;
     asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %1; cvt.f32.f16 %0, lo; }" : "=f"(x) : "r"(h2));
     return x;
+}
+
+// The NaN a NaN code decodes to on the host -- its sign, quiet, and for E5M2 the code's mantissa bits above the
+// quiet bit -- or 0 for a code that is not NaN.  (GPU arithmetic would return the positive canonical NaN; the
+// host keeps a NaN operand's sign and payload, so NaNs are carried around the arithmetic here.)
+__device__ __forceinline__ uint32_t fp8_nan_bits(uint32_t c, bool e5m2)
+{
+    const uint32_t sign = (c & 0x80U) << 24;
+    if (e5m2) return ((c & 0x7cU) == 0x7cU && (c & 3U)) ? (sign | 0x7fc00000U | ((c & 3U) << 21)) : 0U;
+    return (c & 0x7fU) == 0x7fU ? (sign | 0x7fe00000U) : 0U;
 }
 
 // Value i of a state buffer as fp32 (FP8: code x block scale; a second moment is the square of that).
@@ -81,8 +91,10 @@ __device__ __forceinline__ float load_value(const View& s, int64_t i)
         return u2f(((uint32_t) static_cast<const uint16_t*>(s.values)[i] << 16) |
                    ((uint32_t) static_cast<const uint8_t*>(s.aux)[i] << 8));
     default: {
-        const float q = fp8_value(static_cast<const uint8_t*>(s.values)[i], s.v_role != 0);
-        const float x = __fmul_rn(q, static_cast<const float*>(s.aux)[i / s.block]);
+        const uint32_t c = static_cast<const uint8_t*>(s.values)[i];
+        const uint32_t nan = fp8_nan_bits(c, s.v_role != 0);
+        if (nan) return u2f(nan);
+        const float x = __fmul_rn(fp8_value(c, s.v_role != 0), static_cast<const float*>(s.aux)[i / s.block]);
         return s.v_role ? __fmul_rn(x, x) : x;
     }
     }
@@ -99,11 +111,9 @@ __device__ __forceinline__ uint32_t bf16_bits_of(float x)
     return d;
 }
 
-// A value already clamped to the format's finite range (or NaN) -> its FP8 code, nearest-even; a NaN becomes
-// 0x7f with its sign bit, as torch's float8 casts give it.  Zeros keep their sign.
+// A value already clamped to the format's finite range -> its FP8 code, nearest-even.  Zeros keep their sign.
 __device__ __forceinline__ uint32_t fp8_code_of(float q, bool e5m2)
 {
-    if (q != q) return 0x7fU | ((f2u(q) >> 24) & 0x80U);
     uint16_t c2;
     if (e5m2)
         asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c2) : "f"(0.0f), "f"(q));
@@ -140,20 +150,34 @@ __global__ void __launch_bounds__(kThreads) convert_kernel(const __grid_constant
         if (d.dtype == ABX_DT_FP8) {
             // FP8Store.write: a second moment is kept as sqrt(max(v, 0)); the block's scale is absmax / fmax
             // (1 for an all-zero or NaN block); values are divided by it, clamped to +-fmax and cast.
+            // A NaN passes through all of that on the host with its sign and becomes code 0x7f | sign (torch's
+            // float8 casts); it is carried past the arithmetic here.
             const bool v = d.v_role != 0;
             const float fmax = v ? 57344.0f : 448.0f;
             if (v) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) x[k] = __fsqrt_rn(x[k] < 0.0f ? 0.0f : x[k]);
+                for (int k = 0; k < 4; ++k)
+                    if (x[k] == x[k]) x[k] = __fsqrt_rn(x[k] < 0.0f ? 0.0f : x[k]);
             }
             const float amax = warp_absmax_nan(x);
             const float scale = amax > 0.0f ? __fdiv_rn(amax, fmax) : 1.0f;
             uint32_t w = 0;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                float q = __fdiv_rn(x[k], scale);
-                q = q < -fmax ? -fmax : (q > fmax ? fmax : q);   // NaN passes through
-                w |= fp8_code_of(q, v) << (8 * k);
+                uint32_t code;
+                if (x[k] != x[k]) {
+                    code = 0x7fU | ((f2u(x[k]) >> 24) & 0x80U);
+                } else {
+                    float q = __fdiv_rn(x[k], scale);
+                    if (q != q) {
+                        code = 0xffU;   // inf / inf (an infinite value, so an infinite scale): the host's
+                                        // invalid-operation NaN has its sign bit set
+                    } else {
+                        q = q < -fmax ? -fmax : (q > fmax ? fmax : q);
+                        code = fp8_code_of(q, v);
+                    }
+                }
+                w |= code << (8 * k);
             }
             *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(d.values) + i0) = w;   // whole padded block
             if (lane == 0) static_cast<float*>(d.aux)[blk] = scale;

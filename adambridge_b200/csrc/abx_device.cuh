@@ -331,7 +331,7 @@ __device__ __forceinline__ uint32_t enc4_plain(const float (&x)[4], const uint32
 __device__ __forceinline__ bool fast_scale(float s) { return s >= 0x1p-80f && s <= 0x1p100f; }
 
 // IEEE quotients for blocks whose scale is outside the fast range (out of line: rare).
-__device__ __noinline__ float4 div4_ieee(float4 x, float s)
+static __device__ __noinline__ float4 div4_ieee(float4 x, float s)
 {
     return make_float4(__fdiv_rn(x.x, s), __fdiv_rn(x.y, s), __fdiv_rn(x.z, s), __fdiv_rn(x.w, s));
 }

@@ -42,9 +42,9 @@ import torch
 
 from . import native
 from .native import StepCoefficients, mix_seed
-from .precision import FP8_BLOCK, FP32Store, MomentStore, make_master, make_store
+from .precision import StateBuffer
 
-__all__ = ["UpdateEngine", "ParamSlot", "SmallGroup", "StepStats"]
+__all__ = ["UpdateEngine", "ParamSlot", "StepStats"]
 
 log = logging.getLogger("adambridge_b200")
 
@@ -56,8 +56,8 @@ _GRAD_DTYPES = (torch.float32, torch.bfloat16)
 class ParamSlot:
     """Device-side optimizer state for one parameter."""
 
-    __slots__ = ("index", "param", "group", "numel", "step", "master", "out", "m", "v", "submitted", "seg",
-                 "seg_group", "small", "in_place")
+    __slots__ = ("index", "param", "group", "numel", "step", "master", "out", "m", "v", "seg", "seg_group", "small",
+                 "in_place")
 
     def __init__(self, index: int, param: torch.Tensor, group: dict):
         self.index = index
@@ -65,14 +65,13 @@ class ParamSlot:
         self.group = group
         self.numel = param.numel()
         self.step = 0
-        self.master: MomentStore | None = None  # FP32Store (maybe the FP32 parameter itself) or FP24Store
+        self.master: StateBuffer | None = None  # fp32 (maybe viewing the FP32 parameter itself) or fp24
         self.out: torch.Tensor | None = None     # new weights when not written to the parameter directly
-        self.m: MomentStore | None = None
-        self.v: MomentStore | None = None        # None for Lion
-        self.submitted = False
+        self.m: StateBuffer | None = None
+        self.v: StateBuffer | None = None        # None for Lion
         self.seg: native.Segment | None = None   # kernel description of the buffers above
         self.seg_group = None
-        self.small: SmallGroup | None = None
+        self.small = False                       # updated at step_sync with the other small parameters, not hooked
         self.in_place = False                    # the master is the parameter itself (FP32 + fp32 master)
 
     @property
@@ -83,18 +82,6 @@ class ParamSlot:
     def gpu(self):
         """Kept for API parity with the reference (its GPU-resident subset); all state is on the GPU here."""
         return None
-
-
-class SmallGroup:
-    """Small parameters of one device and dtype, updated together at ``step_sync`` by one launch."""
-
-    def __init__(self, slots: list[ParamSlot]):
-        self.slots = slots
-        self.device = slots[0].param.device
-        self.dtype = slots[0].param.dtype
-        for slot in slots:
-            slot.small = self
-        self.total = sum(s.numel for s in slots)
 
 
 @dataclass
@@ -195,12 +182,12 @@ class UpdateEngine:
                 # (delayed updates, deferred write-back), which needs a master separate from the parameter.
                 if (p.dtype == torch.float32 and self.master_precision == "fp32" and not self.may_delay
                         and self.overlap_writeback):
-                    slot.master, slot.in_place = FP32Store.wrap(p.data.view(-1)), True
+                    slot.master, slot.in_place = StateBuffer.viewing(p.data.view(-1)), True
                 else:
-                    slot.master = make_master(self.master_precision, slot.numel, init=p.detach(), device=p.device)
+                    slot.master = StateBuffer.converted(p.detach(), self.master_precision, "p", p.device)
                     slot.in_place = False
-                slot.m = make_store(self.precision, slot.numel, "m", device=p.device)
-                slot.v = None if self.lion else make_store(self.precision, slot.numel, "v", device=p.device)
+                slot.m = StateBuffer.allocate(self.precision, "m", slot.numel, p.device)
+                slot.v = None if self.lion else StateBuffer.allocate(self.precision, "v", slot.numel, p.device)
             slot.seg = None
 
     def initialize(self, slot: ParamSlot, pool=None) -> None:
@@ -211,12 +198,12 @@ class UpdateEngine:
         dev = slot.param.device
         with torch.cuda.device(dev):
             torch.cuda.current_stream(dev).wait_stream(self.stream_for(dev))
-            slot.m = make_store(precision, slot.numel, "m", init=slot.m.to_fp32(), device=dev)
+            slot.m = StateBuffer.converted(slot.m, precision, "m", dev)
             if slot.v is not None:
-                slot.v = make_store(precision, slot.numel, "v", init=slot.v.to_fp32(), device=dev)
+                slot.v = StateBuffer.converted(slot.v, precision, "v", dev)
         slot.seg = None
 
-    def replace_moments(self, slot: ParamSlot, m: MomentStore, v: MomentStore | None) -> None:
+    def replace_moments(self, slot: ParamSlot, m: StateBuffer, v: StateBuffer | None) -> None:
         slot.m, slot.v = m, v
         slot.seg = None
 
@@ -248,21 +235,21 @@ class UpdateEngine:
         seg = slot.seg
         if seg is None:
             seg = native.Segment()
-            p_hi, p_lo = slot.master.native_buffers
+            p_hi, p_lo = slot.master.operands
             seg.p = p_hi.data_ptr()
             seg.p_lo = p_lo.data_ptr() if p_lo is not None else None
-            seg.p_dtype = native.MASTER_CODES[slot.master.precision]
-            m_buf, m_scale = slot.m.native_buffers
+            seg.p_dtype = slot.master.kernel_code
+            m_buf, m_scale = slot.m.operands
             seg.m = m_buf.data_ptr()
             seg.m_scale = m_scale.data_ptr() if m_scale is not None else None
             if slot.v is not None:
-                v_buf, v_scale = slot.v.native_buffers
+                v_buf, v_scale = slot.v.operands
                 seg.v = v_buf.data_ptr()
                 seg.v_scale = v_scale.data_ptr() if v_scale is not None else None
             seg.n = slot.numel
             seg.index = slot.index
             seg.offset = 0
-            seg.mv_dtype = native.MOMENT_CODES[slot.m.precision]
+            seg.mv_dtype = slot.m.kernel_code
             seg.algorithm = native.ALGORITHMS[self.algorithm]
             slot.seg, slot.seg_group = seg, None
         return seg
@@ -283,12 +270,6 @@ class UpdateEngine:
     def submit(self, slot: ParamSlot, grad: torch.Tensor, g_scale: torch.Tensor | None = None) -> None:
         """Enqueue the update of ``slot`` with ``grad`` (called from autograd hooks or ``step``)."""
         self.submit_many([(slot, grad)], g_scale=g_scale)
-
-    def submit_small(self, group: SmallGroup, grads: list) -> list[ParamSlot]:
-        """Enqueue the updates of a SmallGroup's members that have a gradient (one launch)."""
-        items = [(slot, g) for slot, g in zip(group.slots, grads) if g is not None]
-        self.submit_many(items)
-        return [slot for slot, _ in items]
 
     def submit_many(self, items: list[tuple[ParamSlot, torch.Tensor]], g_scale: torch.Tensor | None = None) -> None:
         """Enqueue updates for (slot, grad) pairs: one ``abx_multi_step`` call per device."""
@@ -474,19 +455,19 @@ class UpdateEngine:
         if isinstance(master, torch.Tensor):
             n, p_hi, p_lo, p_code = master.numel(), master, None, native.DT_F32
         else:
-            n, (p_hi, p_lo), p_code = master.numel, master.native_buffers, native.MASTER_CODES[master.precision]
+            n, (p_hi, p_lo), p_code = master.numel, master.operands, master.kernel_code
         if n == 0:
             return
         lion = v is None
-        m_data, m_scale = m.native_buffers
-        v_data, v_scale = (None, None) if lion else v.native_buffers
+        m_data, m_scale = m.operands
+        v_data, v_scale = (None, None) if lion else v.operands
         seg = native.Segment(
             p=p_hi.data_ptr(), p_lo=p_lo.data_ptr() if p_lo is not None else None, p_dtype=p_code,
             g=grad.data_ptr(), m=m_data.data_ptr(), v=v_data.data_ptr() if v_data is not None else None,
             m_scale=m_scale.data_ptr() if m_scale is not None else None,
             v_scale=v_scale.data_ptr() if v_scale is not None else None,
             out=out.data_ptr() if out is not None else None, n=n, g_dtype=native.dtype_code_of(grad.dtype),
-            mv_dtype=native.MOMENT_CODES[m.precision],
+            mv_dtype=m.kernel_code,
             out_dtype=native.DT_NONE if out is None else native.dtype_code_of(out.dtype),
             algorithm=native.ALGORITHMS["lion" if lion else "adamw"])
         hp = self.native.make_hparams(c, seed, self.stochastic)

@@ -25,7 +25,7 @@ import torch
 
 from . import _build
 
-__all__ = ["NativeKernels", "Group", "Segment", "StepCoefficients", "load", "build", "available", "mix_seed",
+__all__ = ["NativeKernels", "Group", "Segment", "State", "StepCoefficients", "load", "build", "available", "mix_seed",
            "SIMD_NAMES", "BuildError", "LIBRARY"]
 
 log = logging.getLogger("adambridge_b200.native")
@@ -61,6 +61,13 @@ class Tensor(ctypes.Structure):
 
     _fields_ = [("data", ctypes.c_void_p), ("n", ctypes.c_int64), ("dtype", ctypes.c_int32),
                 ("reserved", ctypes.c_int32)]
+
+
+class State(ctypes.Structure):
+    """One optimizer-state buffer for abx_convert (abx_state): its planes, format code, FP8 role and block."""
+
+    _fields_ = [("values", ctypes.c_void_p), ("aux", ctypes.c_void_p), ("dtype", ctypes.c_int32),
+                ("role", ctypes.c_int32), ("block", ctypes.c_int64)]
 
 
 class _HParams(ctypes.Structure):
@@ -218,6 +225,8 @@ class NativeKernels:
         lib.abx_launch_count.restype = ctypes.c_uint64
         lib.abx_pipeline_status.restype = ctypes.c_int
         lib.abx_status_word.restype = ctypes.POINTER(ctypes.c_uint)
+        lib.abx_convert.restype = ctypes.c_int
+        lib.abx_convert.argtypes = [ctypes.c_void_p, ctypes.POINTER(State), ctypes.POINTER(State), ctypes.c_int64]
         lib.abx_test_pipeline_fault.restype = ctypes.c_int
         lib.abx_test_pipeline_fault.argtypes = [ctypes.c_int64, ctypes.c_uint32]
         tens = ctypes.POINTER(Tensor)
@@ -387,6 +396,11 @@ class NativeKernels:
         """Failure-path tests only: the next launch skips tile ``tile`` (no copy, no arrival), and every wait
         gives up after ``spin_limit`` polls from now on (0: the default).  See abx_test_pipeline_fault."""
         self._lib.abx_test_pipeline_fault(int(tile), int(spin_limit))
+
+    def convert(self, stream, src: State, dst: State, n: int) -> None:
+        """Enqueue the conversion of n values from state buffer ``src`` to ``dst`` (abx_convert) on ``stream``."""
+        rc = self._lib.abx_convert(_stream_handle(stream), ctypes.byref(src), ctypes.byref(dst), int(n))
+        self._check(rc, "abx_convert")
 
     @staticmethod
     def make_hparams(c: StepCoefficients, seed: int, stochastic: bool) -> _HParams:

@@ -1,463 +1,307 @@
-"""Storage formats of the master weights and the moments, resident in GPU memory.
+"""The optimizer state's storage formats in GPU memory, their checkpoint form, and conversion between them.
 
-Same formats, class names and checkpoint dicts as adambridge's ``precision.py``
-(adambridge/precision.py), but every buffer lives on the parameter's CUDA device so
-the fused kernels read and write it in place:
+Each parameter (or ZeRO shard) owns a master-weight buffer and one moment buffer per moment (AdamW two, Lion
+one).  A :class:`StateBuffer` holds ``numel`` values in one *format*, stored as the planes the update kernels
+address directly::
 
-==========  =================  ====================  ===============
-precision   first moment m     second moment v       bytes / param*
-==========  =================  ====================  ===============
-fp32        FP32               FP32                  12
-bf16        BF16               BF16                  8
-fp8         E4M3 + block scale E5M2 + block scale    ~6.06
-==========  =================  ====================  ===============
+    format  planes                                                  bytes / value   holds
+    fp32    data   float32[numel]                                   4               master, moments
+    bf16    data   bfloat16[numel]                                  2               moments
+    fp8     q      codes[ceil(numel / 128) * 128]: E4M3 of m,       1 + 4/128       moments
+                   E5M2 of sqrt(v) (the role decides)
+            scale  float32 per 128-value block
+    fp24    hi     bfloat16[numel] (the top 16 bits of the fp32)    3               master
+            lo     uint8[numel]    (the next 8 bits)
 
-\\* with an FP32 master weight; an FP24 master (bf16 plane + one byte) takes 3.
+The formats and their checkpoint dicts are the reference's (adambridge/precision.py:1-27, 286-480), so a
+checkpoint written by either side loads in the other.  What differs is where the work happens: the buffers live
+in HBM, and a change of format -- ``set_precision``, a checkpoint saved in another precision or by
+``torch.optim.AdamW``, an fp24 master made from the weights, a decoded master for ``master_params()`` -- is one
+launch of libabx's conversion kernel (``abx_convert``) on the buffer's GPU, with the reference's roundings
+(nearest-even; an FP8 block scaled by its absmax).  Only plane copies ever cross PCIe.
 
-The hot path touches only ``native_buffers``.  ``read`` / ``write`` / ``to_fp32``
-serve format conversion (``set_precision``, checkpoints) and use torch operations
-on the device; their rounding follows the reference's conversions (nearest-even,
-or the lowbias32 stochastic stream keyed by element index).
+A checkpoint is validated in full (:meth:`StateBuffer.from_checkpoint`, :func:`check_master`) before anything
+is loaded, so a mismatched one changes nothing.
 """
 
 from __future__ import annotations
 
-import math
-from abc import ABC, abstractmethod
+from dataclasses import dataclass
 from typing import Any
 
 import torch
 
-__all__ = [
-    "PRECISIONS", "MASTER_PRECISIONS", "FP8_BLOCK", "canonical_precision", "canonical_master_precision",
-    "MomentStore", "FP32Store", "BF16Store", "FP8Store", "FP24Store", "make_store", "make_master",
-    "store_from_state_dict", "check_master_state", "load_master_", "master_to_fp32", "bytes_per_param",
-    "round_to_bf16_stochastic", "round_to_fp8_stochastic", "round_to_fp24_stochastic", "round_to_fp24_nearest_",
-    "moment_seed", "random_bits",
-]
+from . import native
 
-_ALIASES = {"fp32": "fp32", "float32": "fp32", "bf16": "bf16", "bf16_moments": "bf16", "bfloat16": "bf16",
-            "fp8": "fp8", "fp8_moments": "fp8"}
-PRECISIONS = ("fp32", "bf16", "fp8")
-_MASTER_ALIASES = {"fp32": "fp32", "float32": "fp32", "fp24": "fp24", "float24": "fp24"}
-MASTER_PRECISIONS = ("fp32", "fp24")
+__all__ = ["BLOCK", "MOMENT_FORMATS", "MASTER_FORMATS", "StateBuffer", "moment_format", "master_format",
+           "bytes_per_param", "check_master", "check_moment"]
 
-FP8_BLOCK = 128
-_FP8_FORMATS = {
-    # role -> (dtype, max finite value, mantissa bits)   (adambridge/precision.py:79-83)
-    "m": (torch.float8_e4m3fn, 448.0, 3),
-    "v": (torch.float8_e5m2, 57344.0, 2),
+BLOCK = 128                      # FP8 values per block scale (the kernels' block)
+MAX_CHECKPOINT_BLOCK = 1 << 20   # the largest FP8 block a checkpoint may declare
+ROLES = ("m", "v", "p")          # first moment, second moment, master weights
+
+
+@dataclass(frozen=True)
+class _Format:
+    code: int                     # libabx dtype code
+    planes: tuple[str, ...]       # plane names, kernel operand order
+    value_bytes: float            # bytes per stored value
+
+
+_FORMATS = {
+    "fp32": _Format(native.DT_F32, ("data",), 4.0),
+    "bf16": _Format(native.DT_BF16, ("data",), 2.0),
+    "fp8": _Format(native.DT_FP8, ("q", "scale"), 1.0 + 4.0 / BLOCK),
+    "fp24": _Format(native.DT_F24, ("hi", "lo"), 3.0),
 }
+MOMENT_FORMATS = ("fp32", "bf16", "fp8")
+MASTER_FORMATS = ("fp32", "fp24")
+_MOMENT_SPELLINGS = {"fp32": ("fp32", "float32"), "bf16": ("bf16", "bf16_moments", "bfloat16"),
+                     "fp8": ("fp8", "fp8_moments")}
+_MASTER_SPELLINGS = {"fp32": ("fp32", "float32"), "fp24": ("fp24", "float24")}
+_FP8_CODE_DTYPE = {"m": torch.float8_e4m3fn, "v": torch.float8_e5m2}
+_VALUE_DTYPE = {"fp32": torch.float32, "bf16": torch.bfloat16}
 
 
-def canonical_precision(name: str) -> str:
-    try:
-        return _ALIASES[name.lower()]
-    except (KeyError, AttributeError):
-        raise ValueError(f"unknown precision {name!r}; expected one of {sorted(_ALIASES)}") from None
+def _lookup(name: Any, spellings: dict[str, tuple[str, ...]], what: str) -> str:
+    key = name.lower() if isinstance(name, str) else None
+    for fmt, names in spellings.items():
+        if key in names:
+            return fmt
+    accepted = sorted(n for names in spellings.values() for n in names)
+    raise ValueError(f"unknown {what} precision {name!r}; expected one of {accepted}")
 
 
-def canonical_master_precision(name: str) -> str:
-    try:
-        return _MASTER_ALIASES[name.lower()]
-    except (KeyError, AttributeError):
-        raise ValueError(f"unknown master precision {name!r}; expected one of {sorted(_MASTER_ALIASES)}") from None
+def moment_format(name: str) -> str:
+    """The moment format a precision name means ('fp32', 'bf16' / 'bf16_moments', 'fp8' / 'fp8_moments', ...)."""
+    return _lookup(name, _MOMENT_SPELLINGS, "moment")
+
+
+def master_format(name: str) -> str:
+    """The master format a precision name means ('fp32' / 'float32' or 'fp24' / 'float24')."""
+    return _lookup(name, _MASTER_SPELLINGS, "master")
 
 
 def bytes_per_param(precision: str, moments: int = 2, master: str = "fp32") -> float:
-    """Device bytes per parameter for the master + ``moments`` moment vectors (AdamW 2, Lion 1)."""
-    moment = {"fp32": 4.0, "bf16": 2.0, "fp8": 1.0 + 4.0 / FP8_BLOCK}[canonical_precision(precision)]
-    return {"fp32": 4.0, "fp24": 3.0}[canonical_master_precision(master)] + moments * moment
+    """Device bytes per parameter of the master plus ``moments`` moment buffers (AdamW 2, Lion 1)."""
+    return _FORMATS[master_format(master)].value_bytes + moments * _FORMATS[moment_format(precision)].value_bytes
 
 
-# ---------------------------------------------------------------- stochastic rounding (conversions)
-
-def _hash32(x: int) -> int:
-    x &= 0xFFFFFFFF
-    x ^= x >> 16
-    x = (x * 0x7FEB352D) & 0xFFFFFFFF
-    x ^= x >> 15
-    x = (x * 0x846CA68B) & 0xFFFFFFFF
-    x ^= x >> 16
-    return x
+def _blocks(numel: int, block: int = BLOCK) -> int:
+    return max(1, -(-numel // block))
 
 
-def moment_seed(seed: int, role: str) -> int:
-    """32-bit rounding stream of ``role``: 'm', 'v' or 'p' (the fp24 master), as the kernels derive it."""
-    seed &= 0xFFFFFFFF
-    if role == "m":
-        return seed
-    return _hash32(seed ^ (0xA511E9B3 if role == "v" else 0x6C8E9CF5))
+class StateBuffer:
+    """``numel`` optimizer-state values of one role ('m', 'v' or 'p') in one format, as device planes."""
 
+    __slots__ = ("fmt", "role", "numel", "block", "planes")
 
-def _to_i32(value: int) -> int:
-    value &= 0xFFFFFFFF
-    return value - (1 << 32) if value >= 1 << 31 else value
+    def __init__(self, fmt: str, role: str, numel: int, planes: dict[str, torch.Tensor], block: int = BLOCK):
+        if fmt not in _FORMATS or role not in ROLES:
+            raise ValueError(f"no state buffer of format {fmt!r} and role {role!r}")
+        self.fmt, self.role, self.numel, self.block = fmt, role, int(numel), int(block)
+        self.planes = planes
 
-
-def random_bits(offset: int, n: int, seed: int, device: torch.device | str = "cpu") -> torch.Tensor:
-    """lowbias32(index ^ seed) for indices ``offset .. offset+n-1`` as int32 bit patterns."""
-    x = (torch.arange(offset, offset + n, dtype=torch.int64, device=device) & 0xFFFFFFFF)
-    x = x.to(torch.int32) if offset + n <= 1 << 31 else (x - ((x >= 1 << 31).long() << 32)).to(torch.int32)
-    x.bitwise_xor_(_to_i32(seed))
-    x.bitwise_xor_(x.bitwise_right_shift(16).bitwise_and_(0xFFFF))
-    x.mul_(0x7FEB352D)
-    x.bitwise_xor_(x.bitwise_right_shift(15).bitwise_and_(0x1FFFF))
-    x.mul_(_to_i32(0x846CA68B))
-    x.bitwise_xor_(x.bitwise_right_shift(16).bitwise_and_(0xFFFF))
-    return x
-
-
-def _stochastic_truncate_(x: torch.Tensor, dropped_bits: int, offset: int, seed: int) -> torch.Tensor:
-    noise = random_bits(offset, x.numel(), seed, x.device).bitwise_and_((1 << dropped_bits) - 1)
-    x.view(torch.int32).add_(noise).bitwise_and_(-(1 << dropped_bits))
-    return x
-
-
-def round_to_bf16_stochastic(x: torch.Tensor, seed: int, offset: int = 0) -> torch.Tensor:
-    """FP32 ``x`` stochastically rounded to bf16 (``x`` is clobbered)."""
-    return _stochastic_truncate_(x, 16, offset, seed).to(torch.bfloat16)
-
-
-def round_to_fp8_stochastic(x: torch.Tensor, dtype: torch.dtype, seed: int, offset: int = 0) -> torch.Tensor:
-    _, fmax, mbits = next(f for f in _FP8_FORMATS.values() if f[0] == dtype)
-    _stochastic_truncate_(x, 23 - mbits, offset, seed)
-    return x.clamp_(-fmax, fmax).to(dtype)
-
-
-def round_to_fp24_stochastic(x: torch.Tensor, seed: int, offset: int = 0) -> torch.Tensor:
-    return _stochastic_truncate_(x, 8, offset, seed)
-
-
-def round_to_fp24_nearest_(x: torch.Tensor) -> torch.Tensor:
-    """Round FP32 ``x`` in place to its top 24 bits, nearest even; NaN stays NaN."""
-    b = x.view(torch.int32)
-    nan = x.isnan()
-    quiet = b.bitwise_or(0x00400000)
-    b.add_(b.bitwise_right_shift(8).bitwise_and_(1).add_(0x7F)).bitwise_and_(~0xFF)
-    b.copy_(torch.where(nan, quiet, b))
-    return x
-
-
-# ---------------------------------------------------------------- stores
-
-class MomentStore(ABC):
-    """One moment vector (or master) of one parameter, flat, on ``device``."""
-
-    precision: str
-
-    def __init__(self, numel: int, device: torch.device | str | None = None):
-        self.numel = numel
-        self.device = torch.device(device) if device is not None else torch.device("cpu")
-
-    @abstractmethod
-    def read(self, lo: int, hi: int) -> torch.Tensor: ...
-
-    @abstractmethod
-    def write(self, lo: int, hi: int, x: torch.Tensor, seed: int | None = None) -> None: ...
-
-    @abstractmethod
-    def to_fp32(self) -> torch.Tensor: ...
-
-    @property
-    @abstractmethod
-    def nbytes(self) -> int: ...
-
-    @property
-    def native_buffers(self) -> tuple[torch.Tensor, torch.Tensor | None]:
-        """(values or codes, per-block scales or None) in the kernels' layout."""
-        raise NotImplementedError
-
-    @property
-    def chunk_alignment(self) -> int:
-        return 1
-
-    @abstractmethod
-    def state_dict(self) -> dict[str, Any]: ...
-
-
-class FP32Store(MomentStore):
-    precision = "fp32"
-
-    def __init__(self, numel: int, init: torch.Tensor | None = None, device=None):
-        super().__init__(numel, device)
-        self.data = torch.zeros(numel, dtype=torch.float32, device=self.device)
-        if init is not None:
-            self.data.copy_(init.reshape(-1))
+    # ------------------------------------------------------------------ construction
 
     @classmethod
-    def wrap(cls, data: torch.Tensor) -> "FP32Store":
-        """A store over an existing flat FP32 tensor (an FP32 parameter updated in place)."""
-        store = cls.__new__(cls)
-        MomentStore.__init__(store, data.numel(), data.device)
-        store.data = data
-        return store
-
-    def read(self, lo, hi):
-        return self.data[lo:hi]
-
-    def write(self, lo, hi, x, seed=None):
-        dst = self.data[lo:hi]
-        if x.data_ptr() != dst.data_ptr():
-            dst.copy_(x)
-
-    def to_fp32(self):
-        return self.data.clone()
-
-    @property
-    def nbytes(self):
-        return self.data.nbytes
-
-    @property
-    def native_buffers(self):
-        return self.data, None
-
-    def state_dict(self):
-        return {"precision": "fp32", "data": self.data}
-
-
-class BF16Store(MomentStore):
-    precision = "bf16"
-
-    def __init__(self, numel: int, init: torch.Tensor | None = None, device=None):
-        super().__init__(numel, device)
-        self.data = torch.zeros(numel, dtype=torch.bfloat16, device=self.device)
-        if init is not None:
-            self.data.copy_(init.reshape(-1))   # nearest-even
-
-    def read(self, lo, hi):
-        return self.data[lo:hi].float()
-
-    def write(self, lo, hi, x, seed=None):
-        if seed is not None:
-            self.data[lo:hi].copy_(round_to_bf16_stochastic(x.to(self.device), seed, lo))
+    def allocate(cls, fmt: str, role: str, numel: int, device) -> "StateBuffer":
+        """Zero values (FP8: zero codes, unit scales) on ``device``."""
+        dev = torch.device(device)
+        if fmt == "fp8":
+            nb = _blocks(numel)
+            planes = {"q": torch.zeros(nb * BLOCK, dtype=_FP8_CODE_DTYPE["v" if role == "v" else "m"], device=dev),
+                      "scale": torch.ones(nb, dtype=torch.float32, device=dev)}
+        elif fmt == "fp24":
+            planes = {"hi": torch.zeros(numel, dtype=torch.bfloat16, device=dev),
+                      "lo": torch.zeros(numel, dtype=torch.uint8, device=dev)}
         else:
-            self.data[lo:hi].copy_(x)
+            planes = {"data": torch.zeros(numel, dtype=_VALUE_DTYPE[fmt], device=dev)}
+        return cls(fmt, role, numel, planes)
 
-    def to_fp32(self):
-        return self.data.float()
+    @classmethod
+    def viewing(cls, values: torch.Tensor, role: str = "p") -> "StateBuffer":
+        """A buffer over an existing tensor of fp32 or bf16 values (flattened, not copied): an FP32 parameter
+        that is its own master, or values to convert from."""
+        if values.dtype not in (torch.float32, torch.bfloat16):
+            values = values.float()
+        flat = values.detach().reshape(-1)
+        return cls("fp32" if flat.dtype == torch.float32 else "bf16", role, flat.numel(), {"data": flat})
 
-    @property
-    def nbytes(self):
-        return self.data.nbytes
+    @classmethod
+    def converted(cls, src: "StateBuffer | torch.Tensor", fmt: str, role: str, device) -> "StateBuffer":
+        """A new buffer on ``device`` holding ``src``'s values in ``fmt``."""
+        n = src.numel if isinstance(src, StateBuffer) else src.numel()
+        out = cls.allocate(fmt, role, n, device)
+        out.assign(src)
+        return out
 
-    @property
-    def native_buffers(self):
-        return self.data, None
-
-    def state_dict(self):
-        return {"precision": "bf16", "data": self.data}
-
-
-class FP8Store(MomentStore):
-    """FP8 codes with one FP32 scale per ``block`` elements (absmax / format max).  The second moment is kept
-    as sqrt(v), so ``m`` underflows before ``v`` does (adambridge/precision.py:341-418)."""
-
-    precision = "fp8"
-
-    def __init__(self, numel: int, role: str, init: torch.Tensor | None = None, block: int = FP8_BLOCK,
-                 device=None):
-        super().__init__(numel, device)
-        if role not in _FP8_FORMATS:
-            raise ValueError(f"role must be 'm' or 'v', got {role!r}")
-        self.role = role
-        self.block = block
-        self.dtype, self.fmax, _ = _FP8_FORMATS[role]
-        self.sqrt_domain = role == "v"
-        nblocks = max(1, math.ceil(numel / block))
-        self.q = torch.zeros(nblocks * block, dtype=self.dtype, device=self.device)
-        self.scale = torch.ones(nblocks, dtype=torch.float32, device=self.device)
-        if init is not None:
-            self.write(0, numel, init.reshape(-1).to(self.device, torch.float32).clone())
+    # ------------------------------------------------------------------ inspection
 
     @property
-    def chunk_alignment(self):
-        return self.block
-
-    def read(self, lo, hi):
-        b0, b1 = lo // self.block, math.ceil(hi / self.block)
-        x = self.q[b0 * self.block: b1 * self.block].float().view(-1, self.block)
-        x.mul_(self.scale[b0:b1, None])
-        if self.sqrt_domain:
-            x.square_()
-        off = lo - b0 * self.block
-        return x.view(-1)[off: off + hi - lo]
-
-    def write(self, lo, hi, x, seed=None):
-        n = hi - lo
-        b0, b1 = lo // self.block, math.ceil(hi / self.block)
-        x = x.to(self.device, torch.float32)
-        if self.sqrt_domain:
-            x = x.clamp_(min=0).sqrt_()
-        padded = (b1 - b0) * self.block
-        if padded != n:
-            x = torch.nn.functional.pad(x, (0, padded - n))
-        xb = x.view(-1, self.block)
-        amax = xb.abs().amax(dim=1)
-        scale = torch.where(amax > 0, amax / self.fmax, torch.ones_like(amax))
-        xb.div_(scale[:, None])
-        flat = xb.view(-1)
-        if seed is not None:
-            q = round_to_fp8_stochastic(flat, self.dtype, seed, b0 * self.block)
-        else:
-            q = flat.clamp_(-self.fmax, self.fmax).to(self.dtype)
-        self.q[b0 * self.block: b1 * self.block].copy_(q)
-        self.scale[b0:b1].copy_(scale)
-
-    def to_fp32(self):
-        return self.read(0, self.numel).clone()
+    def device(self) -> torch.device:
+        return next(iter(self.planes.values())).device
 
     @property
-    def nbytes(self):
-        return self.q.nbytes + self.scale.nbytes
+    def precision(self) -> str:
+        return self.fmt
 
     @property
-    def native_buffers(self):
-        if self.block != FP8_BLOCK:
-            raise ValueError("the kernels implement the 128-element FP8 block only")
-        return self.q, self.scale
+    def nbytes(self) -> int:
+        return sum(t.nbytes for t in self.planes.values())
 
-    def state_dict(self):
-        return {"precision": "fp8", "role": self.role, "block": self.block, "q": self.q, "scale": self.scale}
+    @property
+    def operands(self) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """(values / codes / hi plane, scales / lo plane or None): what a kernel segment points at."""
+        names = _FORMATS[self.fmt].planes
+        return self.planes[names[0]], (self.planes[names[1]] if len(names) > 1 else None)
 
+    @property
+    def kernel_code(self) -> int:
+        return _FORMATS[self.fmt].code
 
-class FP24Store(MomentStore):
-    """The FP24 master: the top 24 bits of each FP32 value as a bf16 plane ``hi`` and a byte plane ``lo``."""
+    def plane_runs(self) -> list[tuple[torch.Tensor, int, bool]]:
+        """(plane, values per entry, padded to whole blocks) of each plane: how a ZeRO shard's planes map onto the
+        per-parameter planes of a checkpoint."""
+        if self.fmt == "fp8":
+            return [(self.planes["q"], 1, True), (self.planes["scale"], BLOCK, True)]
+        return [(self.planes[name], 1, False) for name in _FORMATS[self.fmt].planes]
 
-    precision = "fp24"
-    INIT_CHUNK = 1 << 24
+    def _abi(self) -> native.State:
+        first, second = self.operands
+        return native.State(first.data_ptr(), second.data_ptr() if second is not None else None, self.kernel_code,
+                            1 if (self.fmt == "fp8" and self.role == "v") else 0, self.block)
 
-    def __init__(self, numel: int, init: torch.Tensor | None = None, device=None):
-        super().__init__(numel, device)
-        self.hi = torch.zeros(numel, dtype=torch.bfloat16, device=self.device)
-        self.lo = torch.zeros(numel, dtype=torch.uint8, device=self.device)
-        if init is not None:
-            self.init_from_(init)
+    def _same_layout(self, other: "StateBuffer") -> bool:
+        if self.fmt != other.fmt:
+            return False
+        return self.fmt != "fp8" or (self.role == other.role and self.block == other.block)
 
-    def init_from_(self, src: torch.Tensor) -> None:
-        src = src.detach().reshape(-1)
-        if src.dtype == torch.bfloat16:
-            self.hi.copy_(src)
-            self.lo.zero_()
+    # ------------------------------------------------------------------ conversion
+
+    def assign(self, src: "StateBuffer | torch.Tensor", stream=None) -> None:
+        """Make this buffer hold ``src``'s values (another buffer, or a tensor of values) in this buffer's format.
+
+        Planes on another device are copied here first; a different format (or FP8 role or block) is converted by
+        libabx's conversion kernel on ``stream`` (default: the device's current stream)."""
+        if isinstance(src, torch.Tensor):
+            src = StateBuffer.viewing(src, self.role)
+        if src.numel != self.numel:
+            raise ValueError(f"state of {src.numel} elements assigned to a buffer of {self.numel} elements")
+        dev = self.device
+        if not dev.type == "cuda":
+            raise ValueError("state buffers are converted on their GPU; this one is on the host")
+        if src.device != dev:
+            src = src.to_device(dev)
+        if self._same_layout(src):
+            for name in _FORMATS[self.fmt].planes:
+                _raw(self.planes[name]).copy_(_raw(src.planes[name]))
             return
-        for lo in range(0, self.numel, self.INIT_CHUNK):
-            hi = min(lo + self.INIT_CHUNK, self.numel)
-            self.write(lo, hi, src[lo:hi].to(self.device, torch.float32, copy=True))
+        with torch.cuda.device(dev):
+            native.load().convert(stream, src._abi(), self._abi(), self.numel)
 
-    def read(self, lo, hi):
-        bits = (self.hi[lo:hi].view(torch.int16).to(torch.int32) & 0xFFFF) << 16
-        bits |= self.lo[lo:hi].to(torch.int32) << 8
-        return bits.view(torch.float32)
+    def to_device(self, device) -> "StateBuffer":
+        """The same planes, copied as bytes to ``device``."""
+        planes = {k: v.to(device, copy=False).contiguous() for k, v in self.planes.items()}
+        return StateBuffer(self.fmt, self.role, self.numel, planes, self.block)
 
-    def write(self, lo, hi, x, seed=None):
-        x = x.to(self.device, torch.float32).contiguous()
-        if seed is not None:
-            round_to_fp24_stochastic(x, seed, lo)
-        else:
-            round_to_fp24_nearest_(x)
-        b = x.view(torch.int32)
-        self.hi[lo:hi].view(torch.int16).copy_((b >> 16).to(torch.int16))
-        self.lo[lo:hi].copy_(((b >> 8) & 0xFF).to(torch.uint8))
+    def to_fp32(self) -> torch.Tensor:
+        """The values as a new flat fp32 tensor on the buffer's GPU (an fp32 buffer: a copy)."""
+        if self.fmt == "fp32":
+            return self.planes["data"].clone()
+        return StateBuffer.converted(self, "fp32", self.role, self.device).planes["data"]
 
-    def to_fp32(self):
-        return self.read(0, self.numel)
+    # ------------------------------------------------------------------ checkpoints
 
-    @property
-    def nbytes(self):
-        return self.hi.nbytes + self.lo.nbytes
+    def checkpoint(self) -> dict[str, Any]:
+        """The reference's dict for this buffer: ``{"precision", <planes>}``, FP8 with its role and block."""
+        d: dict[str, Any] = {"precision": self.fmt}
+        if self.fmt == "fp8":
+            d.update(role=self.role, block=self.block)
+        d.update(self.planes)
+        return d
 
-    @property
-    def native_buffers(self):
-        return self.hi, self.lo
+    @classmethod
+    def from_checkpoint(cls, saved: Any, numel: int, role: str, what: str) -> "StateBuffer":
+        """A checkpoint moment (a store dict, or a plain tensor of values as torch.optim.AdamW saves it) as a
+        buffer over the checkpoint's own tensors, after checking every field; nothing is copied."""
+        check_moment(saved, numel, what)
+        if isinstance(saved, torch.Tensor):
+            return cls.viewing(saved, role)
+        fmt = saved["precision"]
+        if fmt == "fp8":
+            saved_role = saved.get("role", role)
+            planes = {"q": saved["q"].reshape(-1), "scale": saved["scale"].reshape(-1).float()}
+            return cls("fp8", saved_role, numel, planes, block=saved["block"])
+        data = saved["data"].reshape(-1)
+        if data.dtype != _VALUE_DTYPE[fmt]:
+            data = data.to(_VALUE_DTYPE[fmt])
+        return cls(fmt, role, numel, {"data": data})
 
-    def state_dict(self):
-        return {"precision": "fp24", "hi": self.hi, "lo": self.lo}
+    @classmethod
+    def master_from_checkpoint(cls, saved: Any, numel: int, what: str) -> "StateBuffer":
+        """A checkpoint's master weights (a tensor, or an fp32 / fp24 store dict) as a buffer over its tensors."""
+        check_master(saved, numel, what)
+        if isinstance(saved, torch.Tensor):
+            return cls.viewing(saved, "p")
+        if saved["precision"] == "fp24":
+            return cls("fp24", "p", numel, {"hi": saved["hi"].reshape(-1), "lo": saved["lo"].reshape(-1)})
+        return cls.viewing(saved["data"], "p")
 
 
-def make_store(precision: str, numel: int, role: str, init: torch.Tensor | None = None, device=None) -> MomentStore:
-    """Allocate a moment store on ``device``; ``role`` is 'm' or 'v' (picks the FP8 format)."""
-    precision = canonical_precision(precision)
-    if precision == "fp32":
-        return FP32Store(numel, init, device)
-    if precision == "bf16":
-        return BF16Store(numel, init, device)
-    return FP8Store(numel, role, init, device=device)
+def _raw(t: torch.Tensor) -> torch.Tensor:
+    """The same bytes as an integer tensor, so copies move bits and never convert values."""
+    return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
 
 
-def make_master(precision: str, numel: int, init: torch.Tensor | None = None, device=None) -> MomentStore:
-    precision = canonical_master_precision(precision)
-    if precision == "fp24":
-        return FP24Store(numel, init, device)
-    return FP32Store(numel, init, device)
+# ---------------------------------------------------------------------- checkpoint validation
 
-
-def _checked(t: Any, numel: int, what: str) -> torch.Tensor:
+def _tensor_of(t: Any, numel: int, what: str) -> torch.Tensor:
+    """``t`` when it is a tensor of exactly ``numel`` elements; a smaller one would silently broadcast."""
     if not isinstance(t, torch.Tensor):
-        raise ValueError(f"checkpoint {what} is {type(t).__name__}, expected a tensor")
+        raise ValueError(f"checkpoint {what}: expected a tensor, found {type(t).__name__}")
     if t.numel() != numel:
-        raise ValueError(f"checkpoint {what} has {t.numel()} elements, expected {numel} (a different model?)")
+        raise ValueError(f"checkpoint {what}: {t.numel()} elements where this optimizer has {numel} "
+                         "(a checkpoint of another model?)")
     return t
 
 
-def check_master_state(saved: Any, numel: int, what: str) -> None:
-    """Validate a checkpoint's master weights: an FP32 tensor, or an fp32/fp24 store dict."""
+def check_moment(saved: Any, numel: int, what: str) -> None:
+    """Raise ValueError unless ``saved`` is a loadable moment of ``numel`` values: a tensor of values, or an
+    fp32 / bf16 / fp8 store dict whose planes have the sizes its format implies."""
     if isinstance(saved, torch.Tensor):
-        _checked(saved, numel, what)
+        _tensor_of(saved, numel, what)
         return
-    if not isinstance(saved, dict) or saved.get("precision") not in MASTER_PRECISIONS:
-        raise ValueError(f"checkpoint {what}: expected a tensor or an fp32/fp24 store, got "
-                         f"{saved.get('precision') if isinstance(saved, dict) else type(saved).__name__!r}")
-    if saved["precision"] == "fp24":
-        if _checked(saved.get("hi"), numel, f"{what} (hi plane)").dtype != torch.bfloat16:
-            raise ValueError(f"checkpoint {what}: the hi plane must be bfloat16")
-        if _checked(saved.get("lo"), numel, f"{what} (lo plane)").dtype != torch.uint8:
-            raise ValueError(f"checkpoint {what}: the lo plane must be uint8")
-    else:
-        _checked(saved.get("data"), numel, what)
+    fmt = saved.get("precision") if isinstance(saved, dict) else None
+    if fmt not in MOMENT_FORMATS:
+        raise ValueError(f"checkpoint {what}: unknown moment precision {fmt if isinstance(saved, dict) else saved!r}")
+    if fmt != "fp8":
+        _tensor_of(saved.get("data"), numel, what)
+        return
+    if saved.get("role", "m") not in ("m", "v"):
+        raise ValueError(f"checkpoint {what}: unknown FP8 role {saved.get('role')!r}")
+    block = saved.get("block")
+    if isinstance(block, bool) or not isinstance(block, int) or not 0 < block <= MAX_CHECKPOINT_BLOCK:
+        raise ValueError(f"checkpoint {what}: invalid FP8 block size {block!r}")
+    nb = _blocks(numel, block)
+    _tensor_of(saved.get("q"), nb * block, f"{what} (FP8 codes)")
+    _tensor_of(saved.get("scale"), nb, f"{what} (FP8 scales)")
 
 
-def master_to_fp32(saved: Any, numel: int, device=None) -> torch.Tensor:
+def check_master(saved: Any, numel: int, what: str) -> None:
+    """Raise ValueError unless ``saved`` is loadable master weights: a tensor of ``numel`` values, or an fp32 /
+    fp24 store dict (fp24: a bfloat16 hi plane and a uint8 lo plane)."""
     if isinstance(saved, torch.Tensor):
-        return saved.detach().reshape(-1).to(device or saved.device, torch.float32)
-    if saved["precision"] == "fp24":
-        store = FP24Store(numel, device=device or saved["hi"].device)
-        store.hi.copy_(saved["hi"].reshape(-1))
-        store.lo.copy_(saved["lo"].reshape(-1))
-        return store.to_fp32()
-    return saved["data"].detach().reshape(-1).to(device or saved["data"].device, torch.float32)
-
-
-def load_master_(store: MomentStore, saved: Any) -> None:
-    """Load validated checkpoint master weights into ``store`` (converting fp32 <-> fp24)."""
-    if isinstance(store, FP24Store) and isinstance(saved, dict) and saved.get("precision") == "fp24":
-        store.hi.copy_(saved["hi"].reshape(-1))
-        store.lo.copy_(saved["lo"].reshape(-1))
+        _tensor_of(saved, numel, what)
         return
-    x = master_to_fp32(saved, store.numel, store.device)
-    if isinstance(store, FP32Store):
-        store.data.copy_(x)
+    fmt = saved.get("precision") if isinstance(saved, dict) else None
+    if fmt not in MASTER_FORMATS:
+        found = fmt if isinstance(saved, dict) else type(saved).__name__
+        raise ValueError(f"checkpoint {what}: expected a tensor or an fp32 / fp24 master, found precision {found!r}")
+    if fmt == "fp32":
+        _tensor_of(saved.get("data"), numel, what)
         return
-    store.write(0, store.numel, x.clone())
-
-
-def store_from_state_dict(state: dict[str, Any], numel: int, role: str, device=None) -> MomentStore:
-    """Rebuild a moment store from a checkpoint, validating every field first."""
-    if not isinstance(state, dict) or state.get("precision") not in PRECISIONS:
-        raise ValueError("checkpoint moment store has unknown precision "
-                         f"{state.get('precision') if isinstance(state, dict) else state!r}")
-    precision = state["precision"]
-    if precision == "fp8":
-        saved_role, block = state.get("role", role), state.get("block")
-        if saved_role not in _FP8_FORMATS:
-            raise ValueError(f"checkpoint FP8 store has unknown role {saved_role!r}")
-        if not isinstance(block, int) or isinstance(block, bool) or not 0 < block <= 1 << 20:
-            raise ValueError(f"checkpoint FP8 store has invalid block size {block!r}")
-        store = FP8Store(numel, saved_role, block=block, device=device)
-        store.q.copy_(_checked(state.get("q"), store.q.numel(), "FP8 codes"))
-        store.scale.copy_(_checked(state.get("scale"), store.scale.numel(), "FP8 scales"))
-        if saved_role != role or block != FP8_BLOCK:
-            store = FP8Store(numel, role, init=store.to_fp32(), device=device)
-        return store
-    store = make_store(precision, numel, role, device=device)
-    store.data.copy_(_checked(state.get("data"), numel, f"{precision} moments"))
-    return store
+    if _tensor_of(saved.get("hi"), numel, f"{what} (hi plane)").dtype != torch.bfloat16:
+        raise ValueError(f"checkpoint {what}: the fp24 hi plane must be bfloat16")
+    if _tensor_of(saved.get("lo"), numel, f"{what} (lo plane)").dtype != torch.uint8:
+        raise ValueError(f"checkpoint {what}: the fp24 lo plane must be uint8")

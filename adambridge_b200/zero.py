@@ -34,8 +34,7 @@ import torch
 import torch.distributed as dist
 
 from . import native
-from .precision import (FP8Store, FP24Store, FP32Store, _checked, canonical_master_precision, canonical_precision,
-                        check_master_state, load_master_, make_master, make_store, store_from_state_dict)
+from .precision import StateBuffer, check_master, check_moment, master_format, moment_format
 
 __all__ = ["FlatLayout", "Piece", "ZeroAdamBridge", "ZeroLionBridge"]
 
@@ -166,8 +165,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         if not 0.0 <= betas[0] < 1.0 or not 0.0 <= betas[1] < 1.0:
             raise ValueError(f"invalid betas: {betas}")
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
-        self.precision = canonical_precision(precision)
-        self.master_precision = canonical_master_precision(master_precision)
+        self.precision = moment_format(precision)
+        self.master_precision = master_format(master_precision)
         self.stochastic = stochastic_rounding
         self.seed = seed
         self.max_ctas = max_ctas
@@ -216,10 +215,10 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 p.data = self.flat_weights[a:b].view(p.shape)
             self._pieces = L.pieces(self.rank)
             master_init = torch.cat([self.flat_weights[slice(*L.rank_range(r, self.rank))] for r in range(L.rounds)])
-            self.master = make_master(self.master_precision, L.shard_numel, init=master_init, device=dev)
+            self.master = StateBuffer.converted(master_init, self.master_precision, "p", dev)
             del master_init
-            self.m = make_store(self.precision, L.shard_numel, "m", device=dev)
-            self.v = None if self._algorithm == "lion" else make_store(self.precision, L.shard_numel, "v", device=dev)
+            self.m = StateBuffer.allocate(self.precision, "m", L.shard_numel, dev)
+            self.v = None if self._algorithm == "lion" else StateBuffer.allocate(self.precision, "v", L.shard_numel, dev)
             self.grad_shard = torch.zeros(L.shard_numel, dtype=self.grad_dtype, device=dev)
         self._flat_grads: torch.Tensor | None = None
         self.step_count = 0
@@ -280,9 +279,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     def _build_segments(self, weights: torch.Tensor) -> list[ctypes.Array]:
         """One segment array per round, pointing into this rank's state and the flat weight buffer ``weights``."""
-        p_hi, p_lo = self.master.native_buffers
-        m_buf, m_scale = self.m.native_buffers
-        v_buf, v_scale = (None, None) if self.v is None else self.v.native_buffers
+        p_hi, p_lo = self.master.operands
+        m_buf, m_scale = self.m.operands
+        v_buf, v_scale = (None, None) if self.v is None else self.v.operands
         p_es = p_hi.element_size()
         m_es = m_buf.element_size()
         out_es = weights.element_size()
@@ -294,7 +293,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 s = native.Segment()
                 s.p = p_hi.data_ptr() + pc.local_lo * p_es
                 s.p_lo = p_lo.data_ptr() + pc.local_lo if p_lo is not None else None
-                s.p_dtype = native.MASTER_CODES[self.master.precision]
+                s.p_dtype = self.master.kernel_code
                 s.g = self.grad_shard.data_ptr() + pc.local_lo * g_es
                 s.g_dtype = native.dtype_code_of(self.grad_dtype)
                 s.m = m_buf.data_ptr() + pc.local_lo * m_es
@@ -307,7 +306,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 s.n = pc.n
                 s.offset = pc.t_lo
                 s.index = pc.index
-                s.mv_dtype = native.MOMENT_CODES[self.m.precision]
+                s.mv_dtype = self.m.kernel_code
                 s.algorithm = native.ALGORITHMS[self._algorithm]
                 s.group = ctypes.pointer(self._groups[self._group_of[pc.index]])
                 self._seg_objs.append(s)
@@ -741,15 +740,6 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     CKPT_ENTRIES = 1 << 25   # shard entries gathered per collective: bounds the temporary buffers
 
     @staticmethod
-    def _planes(store) -> list[tuple[torch.Tensor, int, bool]]:
-        """A store's arrays as (tensor, unit, padded) in the sense of :meth:`FlatLayout.shard_runs`."""
-        if isinstance(store, FP8Store):
-            return [(store.q, 1, True), (store.scale, ALIGN, True)]
-        if isinstance(store, FP24Store):
-            return [(store.hi, 1, False), (store.lo, 1, False)]
-        return [(store.data, 1, False)]
-
-    @staticmethod
     def _raw(t: torch.Tensor) -> torch.Tensor:
         """Same bytes as an integer tensor (collectives and copies move bits, never convert values)."""
         return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
@@ -791,20 +781,21 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         sd["state"] = {}
         keep = not rank0_only or self.rank == 0
         L = self.layout
-        masters = [make_master(self.master_precision, n, device="cpu") for n in L.numels]
-        stores = [("exp_avg", self.m, [make_store(self.precision, n, "m", device="cpu") for n in L.numels])]
+        masters = [StateBuffer.allocate(self.master_precision, "p", n, "cpu") for n in L.numels]
+        stores = [("exp_avg", self.m, [StateBuffer.allocate(self.precision, "m", n, "cpu") for n in L.numels])]
         if self.v is not None:
-            stores.append(("exp_avg_sq", self.v, [make_store(self.precision, n, "v", device="cpu") for n in L.numels]))
+            stores.append(("exp_avg_sq", self.v,
+                           [StateBuffer.allocate(self.precision, "v", n, "cpu") for n in L.numels]))
         for shard_store, per_param in [(self.master, masters)] + [(st, pp) for _, st, pp in stores]:
-            for j, (plane, unit, padded) in enumerate(self._planes(shard_store)):
-                self._gather_plane(plane, [self._planes(p)[j][0] for p in per_param], unit, padded, keep)
+            for j, (plane, unit, padded) in enumerate(shard_store.plane_runs()):
+                self._gather_plane(plane, [p.plane_runs()[j][0] for p in per_param], unit, padded, keep)
         if keep and self.step_count > 0:
             for i in range(len(self._params)):
                 m = masters[i]
                 st = sd["state"][i] = {"step": self.step_count,
-                                       "master": m.data if isinstance(m, FP32Store) else m.state_dict()}
+                                       "master": m.planes["data"] if m.fmt == "fp32" else m.checkpoint()}
                 for key, _, per_param in stores:
-                    st[key] = per_param[i].state_dict()
+                    st[key] = per_param[i].checkpoint()
         sd["adambridge"] = {"precision": self.precision, "master_precision": self.master_precision, "format": 1,
                             "algorithm": self._algorithm}
         return sd
@@ -823,10 +814,10 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                                  f"0..{len(self._params) - 1}")
             numel = L.numels[index]
             if st.get("master") is not None:
-                check_master_state(st["master"], numel, f"master weights of parameter {index}")
+                check_master(st["master"], numel, f"master weights of parameter {index}")
             for key in ("exp_avg", "exp_avg_sq"):
                 if key in st:
-                    _check_moment_state(st[key], numel, f"{key} of parameter {index}")
+                    check_moment(st[key], numel, f"{key} of parameter {index}")
             if "exp_avg" not in st or (not lion and "exp_avg_sq" not in st):
                 raise ValueError("checkpoint has no exp_avg / exp_avg_sq (saved by LionBridge?); AdamW needs both")
         if saved and len(saved) != len(self._params):
@@ -845,7 +836,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 runs.setdefault((unit, padded, index), []).append((p_lo, s_lo, length))
 
         def scatter(shard_store, param_store, index):
-            for (plane, unit, padded), (src, _, _) in zip(self._planes(shard_store), self._planes(param_store)):
+            for (plane, unit, padded), (src, _, _) in zip(shard_store.plane_runs(), param_store.plane_runs()):
                 raw, rsrc = self._raw(plane), self._raw(src)
                 for p_lo, s_lo, length in runs.get((unit, padded, index), []):
                     raw[s_lo:s_lo + length].copy_(rsrc[p_lo:p_lo + length])
@@ -854,8 +845,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             for index, st in saved.items():
                 numel = L.numels[index]
                 if st.get("master") is not None:
-                    master = make_master(self.master_precision, numel, device=dev)
-                    load_master_(master, st["master"])
+                    saved_master = StateBuffer.master_from_checkpoint(st["master"], numel, "master weights")
+                    master = StateBuffer.converted(saved_master, self.master_precision, "p", dev)
                     scatter(self.master, master, index)
                 for key, shard_store, role in (("exp_avg", self.m, "m"), ("exp_avg_sq", self.v, "v")):
                     if shard_store is None:
@@ -865,32 +856,10 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             self.step_count = steps.pop()
         torch.cuda.synchronize(dev)
 
-    def _load_store(self, saved, numel: int, role: str, device):
-        if isinstance(saved, torch.Tensor):  # torch.optim.AdamW layout
-            return make_store(self.precision, numel, role, init=saved.to(device, torch.float32), device=device)
-        store = store_from_state_dict(saved, numel, role, device=device)
-        if store.precision != self.precision:
-            store = make_store(self.precision, numel, role, init=store.to_fp32(), device=device)
-        return store
-
-
-def _check_moment_state(saved: Any, numel: int, what: str) -> None:
-    """Sizes of a checkpoint's moment store (a tensor, or an fp32/bf16/fp8 store dict), checked before anything
-    is loaded, so a mismatched checkpoint changes nothing."""
-    if isinstance(saved, torch.Tensor):
-        _checked(saved, numel, what)
-        return
-    if not isinstance(saved, dict) or saved.get("precision") not in ("fp32", "bf16", "fp8"):
-        raise ValueError(f"checkpoint {what}: unknown moment store")
-    if saved["precision"] != "fp8":
-        _checked(saved.get("data"), numel, what)
-        return
-    block = saved.get("block")
-    if not isinstance(block, int) or isinstance(block, bool) or not 0 < block <= 1 << 20:
-        raise ValueError(f"checkpoint {what}: invalid FP8 block size {block!r}")
-    nblocks = max(1, -(-numel // block))
-    _checked(saved.get("q"), nblocks * block, f"{what} (FP8 codes)")
-    _checked(saved.get("scale"), nblocks, f"{what} (FP8 scales)")
+    def _load_store(self, saved, numel: int, role: str, device) -> StateBuffer:
+        """A checkpoint moment (store dict or AdamW tensor) converted to this optimizer's precision on ``device``."""
+        return StateBuffer.converted(StateBuffer.from_checkpoint(saved, numel, role, "moment"), self.precision, role,
+                                     device)
 
 
 class ZeroLionBridge(ZeroAdamBridge):

@@ -521,11 +521,11 @@ def sharded_parity(args, world: int, rank: int, dev) -> dict:
             checked[1] += (bits(zp.detach()) != bits(ap.detach())).sum()
         zstores = [("master", zopt.master), ("m", zopt.m)] + ([] if zopt.v is None else [("v", zopt.v)])
         for pc in pieces:
-            slot = aopt._ordered[pc.index]
+            slot = aopt.slots[pc.index]
             for name, zst in zstores:
                 ast = getattr(slot, name)
-                zbuf, zsc = zst.native_buffers
-                abuf, asc = ast.native_buffers
+                zbuf, zsc = zst.operands
+                abuf, asc = ast.operands
                 for a, b in ((zbuf[pc.local_lo:pc.local_lo + pc.n], abuf[pc.t_lo:pc.t_hi]),
                              (zsc[pc.local_lo // 128:-(-(pc.local_lo + pc.n) // 128)] if zsc is not None else None,
                               asc[pc.t_lo // 128:-(-pc.t_hi // 128)] if asc is not None else None)):

@@ -75,27 +75,33 @@ def fp8_code(q, role: str) -> np.ndarray:
     ab = a.view(np.uint32).astype(np.uint64)
     r = ab + ((1 << (drop - 1)) - 1) + ((ab >> drop) & 1)
     exp = (r >> 23).astype(np.int64) - 127 + bias
-    normal = ((exp << mbits) | ((r >> drop) & ((1 << mbits) - 1))).astype(np.uint32)
+    mant = ((r >> drop) & ((1 << mbits) - 1)).astype(np.int64)
+    normal = np.where(exp > 0, (exp << mbits) | mant, 0).astype(np.uint32)
     code = np.where(a < np.float32(2.0 ** (1 - bias)), sub, normal)
     code = np.where(np.isnan(q), np.uint32(0x7F), code)
     return ((code | sign) & 0xFF).astype(np.uint8)
 
 
 def fp8_value(codes, role: str) -> np.ndarray:
-    """Exact value of every code (E4M3: 0x7f/0xff NaN; E5M2: exponent 31 is inf or NaN)."""
+    """Exact value of every code (E4M3: 0x7f/0xff NaN; E5M2: exponent 31 is inf or NaN).  A NaN code gives the
+    quiet NaN the host's conversion gives -- its sign, and E5M2's mantissa bits above the quiet bit."""
     f = FP8[role]
     mbits, bias = f["mbits"], f["bias"]
     c = np.asarray(codes, np.uint8).astype(np.int64)
-    s = np.where(c & 0x80, -1.0, 1.0)
     e = (c >> mbits) & ((1 << (7 - mbits)) - 1)
     m = c & ((1 << mbits) - 1)
     mag = np.where(e == 0, m * 2.0 ** (1 - bias - mbits), (1.0 + m / 2.0 ** mbits) * 2.0 ** (e - bias))
     if role == "m":
-        mag = np.where((c & 0x7F) == 0x7F, np.nan, mag)
+        nan = (c & 0x7F) == 0x7F
+        nan_bits = np.full(c.shape, 0x7FE00000, np.int64)
     else:
         top = e == (1 << (7 - mbits)) - 1
-        mag = np.where(top, np.where(m == 0, np.inf, np.nan), mag)
-    return (s * mag).astype(np.float32)
+        mag = np.where(top & (m == 0), np.inf, mag)
+        nan = top & (m != 0)
+        nan_bits = 0x7FC00000 | (m << 21)
+    val = np.copysign(mag, np.where(c & 0x80, -1.0, 1.0)).astype(np.float32)
+    bits = np.where(nan, nan_bits | ((c & 0x80) << 24), val.view(np.uint32).astype(np.int64))
+    return bits.astype(np.uint32).view(np.float32)
 
 
 def fp8_encode(x, role: str) -> tuple[np.ndarray, np.ndarray]:

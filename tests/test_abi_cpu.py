@@ -155,3 +155,25 @@ def test_product_loader_fails_loudly_without_library(tmp_path, monkeypatch):
     monkeypatch.setattr(native, "_loaded", None)
     with pytest.raises(native.BuildError):
         native.load()
+
+
+def test_convert_rejects_bad_arguments_before_touching_the_device(kernels):
+    """abx_convert checks formats, roles, blocks, pointers and alignment before any CUDA call (so on a machine
+    without a GPU every rejection still comes back; the addresses are never dereferenced)."""
+    from adambridge_b200 import native
+    vals, codes, scales = 0x10000, 0x20000, 0x30000
+    src = native.State(vals, None, native.DT_F32, 0, 1)
+    cases = [(native.State(codes, None, native.DT_FP8, 0, 128), -7),         # FP8 without scales
+             (native.State(codes, scales, native.DT_FP8, 0, 64), -1),        # a destination block other than 128
+             (native.State(codes, scales, native.DT_FP8, 2, 128), -1),       # unknown role
+             (native.State(codes, scales, 9, 0, 128), -4),                   # unknown format
+             (native.State(None, None, native.DT_F32, 0, 1), -2),            # no values
+             (native.State(vals + 2, None, native.DT_F32, 0, 1), -21),       # fp32 values not 4-byte aligned
+             (native.State(codes, None, native.DT_F24, 0, 1), -7)]           # fp24 without its lo plane
+    for dst, code in cases:
+        assert kernels._lib.abx_convert(None, ctypes.byref(src), ctypes.byref(dst), 256) == code
+    bad_src = native.State(codes, scales, native.DT_FP8, 0, 0)               # a source block of 0
+    ok_dst = native.State(vals, None, native.DT_F32, 0, 1)
+    assert kernels._lib.abx_convert(None, ctypes.byref(bad_src), ctypes.byref(ok_dst), 256) == -1
+    assert kernels._lib.abx_convert(None, ctypes.byref(src), ctypes.byref(ok_dst), -1) == -1
+    assert kernels._lib.abx_convert(None, ctypes.byref(src), ctypes.byref(ok_dst), 0) == 0

@@ -84,11 +84,11 @@ def _assert_slot_matches(hs: O.HostSegment, p: torch.Tensor, slot, mv: int) -> N
     got = hs.clone()
     if "out" in got.buffers:
         got.buffers["out"][:] = p.detach().reshape(-1).view(torch.int16).cpu().numpy().view(np.uint16)
-    got.buffers["p"][:] = (p.detach().reshape(-1) if slot.in_place else slot.master.data).cpu().numpy()
+    got.buffers["p"][:] = (p.detach().reshape(-1) if slot.in_place else slot.master.planes["data"]).cpu().numpy()
     for name, store in (("m", slot.m), ("v", slot.v)):
         if mv == O.DT_FP8:
-            got.buffers[name][:] = store.q.view(torch.uint8).cpu().numpy()
-            got.buffers[f"{name}_scale"][:] = store.scale.cpu().numpy()
+            got.buffers[name][:] = store.planes["q"].view(torch.uint8).cpu().numpy()
+            got.buffers[f"{name}_scale"][:] = store.planes["scale"].cpu().numpy()
         elif mv == O.DT_BF16:
             got.buffers[name][:] = store.data.view(torch.int16).cpu().numpy().view(np.uint16)
         else:
@@ -115,7 +115,7 @@ def test_c1_flat_fp32_tensor_ten_steps():
         opt.step()
         assert orc.multi_step([hs.ctype(group)], O.SIMD_AVX512) == 0
     torch.cuda.synchronize()
-    _assert_slot_matches(hs, p, opt._ordered[0], O.DT_F32)
+    _assert_slot_matches(hs, p, opt.slots[0], O.DT_F32)
     opt.close()
 
 
@@ -146,7 +146,7 @@ def test_c2_qwen05b_bf16_moments_cosine_lr_50_steps():
         sched.step()
     torch.cuda.synchronize()
     for i, hs in host.items():
-        _assert_slot_matches(hs, params[i], opt._ordered[i], O.DT_BF16)
+        _assert_slot_matches(hs, params[i], opt.slots[i], O.DT_BF16)
     opt.close()
 
 
@@ -184,5 +184,5 @@ def test_c3_llama15b_fp8_moments_with_fused_clip():
         opt.zero_grad()
     torch.cuda.synchronize()
     for i, hs in host.items():
-        _assert_slot_matches(hs, params[i], opt._ordered[i], O.DT_FP8)
+        _assert_slot_matches(hs, params[i], opt.slots[i], O.DT_FP8)
     opt.close()

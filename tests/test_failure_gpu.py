@@ -77,7 +77,7 @@ def test_status_word_is_readable_without_synchronizing(fault):
     assert not fault.status_pending()
     fault.test_pipeline_fault(3, SHORT_LIMIT)
     p.grad = torch.randn_like(p)
-    opt._submit_remaining()                         # the update alone, no step_sync check
+    opt._enqueue(opt._outstanding(small=None))     # the update alone, no step_sync check
     torch.cuda.synchronize()
     assert fault.status_pending()                   # read from host memory, no CUDA call
     bits = fault.pipeline_status()

@@ -167,20 +167,20 @@ def test_public_api_bit_exact_with_oracle(algo, precision, master):
         opt.step()
         assert orc.multi_step([hs.ctype(group) for hs in host], O.SIMD_AVX512) == 0
     torch.cuda.synchronize()
-    for hs, p, slot in zip(host, params, opt._ordered):
+    for hs, p, slot in zip(host, params, opt.slots):
         got = hs.clone()
         got.buffers["out"][:] = p.detach().reshape(-1).view(torch.int16).cpu().numpy().view(np.uint16)
         if pt == O.DT_F24:
-            got.buffers["p"][:] = slot.master.hi.view(torch.int16).cpu().numpy().view(np.uint16)
-            got.buffers["p_lo"][:] = slot.master.lo.cpu().numpy()
+            got.buffers["p"][:] = slot.master.planes["hi"].view(torch.int16).cpu().numpy().view(np.uint16)
+            got.buffers["p_lo"][:] = slot.master.planes["lo"].cpu().numpy()
         else:
-            got.buffers["p"][:] = slot.master.data.cpu().numpy()
+            got.buffers["p"][:] = slot.master.planes["data"].cpu().numpy()
         for name, store in (("m", slot.m), ("v", slot.v)):
             if store is None:
                 continue
             if mv == O.DT_FP8:
-                got.buffers[name][:] = store.q.view(torch.uint8).cpu().numpy()
-                got.buffers[f"{name}_scale"][:] = store.scale.cpu().numpy()
+                got.buffers[name][:] = store.planes["q"].view(torch.uint8).cpu().numpy()
+                got.buffers[f"{name}_scale"][:] = store.planes["scale"].cpu().numpy()
             elif mv == O.DT_BF16:
                 got.buffers[name][:] = store.data.view(torch.int16).cpu().numpy().view(np.uint16)
             else:
@@ -256,7 +256,7 @@ def test_delayed_updates_match_one_step_stale_adamw(warmup):
     want_losses, want = _stale_reference(copy.deepcopy(model), 10, lambda ps: torch.optim.AdamW(ps, lr=3e-3), warmup)
     opt = ab.AdamBridge(model.parameters(), lr=3e-3, delay_updates=True, delay_warmup_steps=warmup,
                         small_param_threshold=2000).attach_hooks(model)
-    assert any(s.small is not None for s in opt._ordered) and any(s.small is None for s in opt._ordered)
+    assert any(s.small for s in opt.slots) and any(not s.small for s in opt.slots)
     losses = []
     for k in range(1, 11):
         loss = lm_loss(model, k)
@@ -383,10 +383,10 @@ def test_set_precision_between_steps():
         lm_loss(model, step).backward()
         opt.step()
         opt.zero_grad()
-    before = [s.m.to_fp32().clone() for s in opt._ordered]
+    before = [s.m.to_fp32().clone() for s in opt.slots]
     opt.set_precision("bf16")
-    assert opt.precision == "bf16" and all(s.m.precision == "bf16" for s in opt._ordered)
-    for b, s in zip(before, opt._ordered):
+    assert opt.precision == "bf16" and all(s.m.precision == "bf16" for s in opt.slots)
+    for b, s in zip(before, opt.slots):
         assert torch.equal(s.m.to_fp32(), b.to(torch.bfloat16).float())
     lm_loss(model, 3).backward()
     opt.step()
