@@ -545,6 +545,48 @@ def sharded_parity(args, world: int, rank: int, dev) -> dict:
             "gather": "fused peer stores" if world > 1 and args.gather != "nccl" else ("nccl" if world > 1 else None)}
 
 
+def host_link_gbs(host_g, host_w, opt, world: int, dev, iters: int = 3) -> dict:
+    """What the host link alone moves for this rank, every rank copying at once (the same pinned buffers and
+    bytes as the end-to-end step, no update): host->device, device->host, and both directions together.  GB/s
+    per rank, the slowest rank's time; the end-to-end step cannot beat the 'both' figure."""
+    import torch
+    import torch.distributed as dist
+
+    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    src_w = opt.flat_weights[:host_w.numel()]
+
+    def timed(up: bool, down: bool) -> float:
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        cur = torch.cuda.current_stream(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        for s in (h2d_s, d2h_s):
+            s.wait_event(a)
+        for _ in range(iters):
+            if up:
+                with torch.cuda.stream(h2d_s):
+                    opt.grad_shard.copy_(host_g, non_blocking=True)
+            if down:
+                with torch.cuda.stream(d2h_s):
+                    host_w.copy_(src_w, non_blocking=True)
+        cur.wait_stream(h2d_s)
+        cur.wait_stream(d2h_s)
+        b.record(cur)
+        torch.cuda.synchronize(dev)
+        ms = torch.tensor([a.elapsed_time(b) / iters], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return ms.item()
+
+    gb = host_g.numel() * host_g.element_size() / 1e9
+    up, down, both = timed(True, False), timed(False, True), timed(True, True)
+    return {"h2d_gbs": round(gb / (up / 1e3), 1), "d2h_gbs": round(gb / (down / 1e3), 1),
+            "both_directions_gbs_each": round(gb / (both / 1e3), 1), "ranks_copying": world,
+            "basis": f"{gb:.2f} GB each way per rank from/to pinned host memory, CUDA events, max over ranks"}
+
+
 def nccl_allgather_gbs(opt, world: int, dev, iters: int = 5) -> float:
     """NVLink ingress per rank (GB/s) that NCCL's in-place all-gather reaches on the step's own weight buffer
     (every rank receives (world - 1) x its shard): the reference rate for the fused all-gather."""
@@ -682,7 +724,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
         e_ms = e_ms.item()
-        e2e = {"value": round(n_params / (e_ms / 1e3) / 1e9, 4), "unit": "Gparams/s",
+        link = host_link_gbs(host_g, host_w, opt, world, dev)
+        e2e = {"value": round(n_params / (e_ms / 1e3) / 1e9, 4), "unit": "Gparams/s", "host_link": link,
                "h2d_bytes_per_step": host_g.numel() * host_g.element_size(),
                "d2h_bytes_per_step": host_w.numel() * host_w.element_size(), "ms_per_step": round(e_ms, 3),
                "path": "ZeroAdamBridge.step_shard(host gradient shard, weights_out=host weight shard): every step "

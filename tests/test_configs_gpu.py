@@ -90,9 +90,9 @@ def _assert_slot_matches(hs: O.HostSegment, p: torch.Tensor, slot, mv: int) -> N
             got.buffers[name][:] = store.planes["q"].view(torch.uint8).cpu().numpy()
             got.buffers[f"{name}_scale"][:] = store.planes["scale"].cpu().numpy()
         elif mv == O.DT_BF16:
-            got.buffers[name][:] = store.data.view(torch.int16).cpu().numpy().view(np.uint16)
+            got.buffers[name][:] = store.planes["data"].view(torch.int16).cpu().numpy().view(np.uint16)
         else:
-            got.buffers[name][:] = store.data.cpu().numpy()
+            got.buffers[name][:] = store.planes["data"].cpu().numpy()
     assert got.mismatches(hs) == {}, (slot.index, got.mismatches(hs))
 
 
