@@ -94,7 +94,10 @@ __device__ __forceinline__ float load_value(const View& s, int64_t i)
         const uint32_t c = static_cast<const uint8_t*>(s.values)[i];
         const uint32_t nan = fp8_nan_bits(c, s.v_role != 0);
         if (nan) return u2f(nan);
-        const float x = __fmul_rn(fp8_value(c, s.v_role != 0), static_cast<const float*>(s.aux)[i / s.block]);
+        const float sc = static_cast<const float*>(s.aux)[i / s.block];
+        float x = __fmul_rn(fp8_value(c, s.v_role != 0), sc);
+        if (x != x)   // a NaN scale propagates, quieted; 0 x inf is the host's default NaN, whose sign bit is set
+            return sc != sc ? u2f(f2u(sc) | 0x00400000U) : u2f(0xffc00000U);
         return s.v_role ? __fmul_rn(x, x) : x;
     }
     }
