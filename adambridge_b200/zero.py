@@ -246,6 +246,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._hook_handles: list = []
         self._clip_coef: torch.Tensor | None = None
         self._norm_state = None
+        self._update_in_backward = False
+        self._rounds_updated: set[int] = set()   # hook mode: rounds this step already updated during backward
 
     # ------------------------------------------------------------------ fused all-gather
 
@@ -406,7 +408,14 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 loss = closure()
         if self._hooked:
             self._finish_hooked_reduce()
-        if self._clip_coef is not None:
+        if self._rounds_updated:
+            # hook mode, updated during backward: whatever round is left, then the end of the step
+            cur = torch.cuda.current_stream(self.device)
+            for r in range(self.layout.rounds):
+                if r not in self._rounds_updated:
+                    self._backward_update_round(r)
+            self._finish_update(cur, delayed=False)
+        elif self._clip_coef is not None:
             coef, self._clip_coef = self._clip_coef, None
             self._run(None, g_scale=coef, synced=True)
         elif self._hooked:
@@ -418,15 +427,22 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     # ------------------------------------------------------------------ gradients reduced during backward
 
-    def attach_hooks(self, model: torch.nn.Module | None = None) -> "ZeroAdamBridge":
-        """Reduce-scatter the gradients during backward (the data-parallel gradient path).
+    def attach_hooks(self, model: torch.nn.Module | None = None,
+                     update_in_backward: bool = True) -> "ZeroAdamBridge":
+        """Reduce-scatter the gradients during backward (the data-parallel gradient path) and, with
+        ``update_in_backward``, update the weights during backward too.
 
         A post-accumulate-grad hook copies each parameter's finished gradient into the flat gradient buffer
         (and, with ``release_grads``, frees ``p.grad``); when every parameter overlapping a round of the flat
         layout has arrived, that round's reduce-scatter (mean) starts on the comm stream, so it overlaps the
-        rest of backward -- backward runs roughly in reverse parameter order, so the last rounds go first.
-        ``step()`` then waits for the reduce-scatters and updates.  The overlap is per round: construct the
-        optimizer with ``rounds`` > 1 for it.  Every parameter must receive exactly one gradient per step."""
+        rest of backward -- backward runs roughly in reverse parameter order, so the last rounds go first.  With
+        ``update_in_backward`` (the reference's hook mode: each update as soon as its gradient is ready) the
+        round's update kernel -- with its fused all-gather -- follows its reduce-scatter right away on the
+        update stream, and ``step()`` only ends the step; otherwise ``step()`` updates every round.  Delayed
+        updates and :meth:`clip_grad_norm_` (which needs every gradient before any update) update at ``step()``:
+        pass ``update_in_backward=False`` to clip.  The overlap is per round: construct the optimizer with
+        ``rounds`` > 1 for it.  Every parameter must receive exactly one gradient per step."""
+        self._update_in_backward = bool(update_in_backward)
         if self._hooked:
             return self
         wanted = None if model is None else {id(p) for p in model.parameters()}
@@ -457,6 +473,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 self._round_waiting[r] += 1
         self._arrived = [False] * len(self._params)
         self._reduced = [False] * L.rounds
+        self._rounds_updated = set()
 
     def _on_grad_ready(self, p: torch.Tensor) -> None:
         i = self._index_of[id(p)]
@@ -473,6 +490,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             self._round_waiting[r] -= 1
             if self._round_waiting[r] == 0:
                 self._reduce_round(r)
+                if self._updates_in_backward():
+                    self._backward_update_round(r)
 
     def _reduce_round(self, r: int) -> None:
         """Reduce-scatter round ``r`` of the flat gradients into this rank's shard (comm stream, ordered after
@@ -574,6 +593,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         if float(norm_type) != 2.0:
             raise ValueError("clip_grad_norm_ computes the L2 norm (norm_type=2) only")
         cur = torch.cuda.current_stream(self.device)
+        if self._rounds_updated:
+            raise RuntimeError("clip_grad_norm_ after the hooks already updated rounds during backward: attach the "
+                               "hooks with update_in_backward=False to clip")
         if self._hooked:   # reduced during backward
             self._finish_hooked_reduce()
             self._update_stream.wait_stream(cur)
@@ -646,9 +668,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         delayed = self._delayed()
         if delayed:
             self._ensure_shadow()
-        weights = self._shadow if delayed else self.flat_weights
-        segs = self._shadow_segs if delayed else self._segs
-        deltas = self._shadow_deltas if delayed else self._peer_deltas
+        target = self._target(delayed)
         self._refresh()
         upd, comm = self._update_stream, self._comm_stream
         p2p = self._peer_deltas is not None
@@ -683,43 +703,82 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                             dist.reduce_scatter_tensor(shard, src, op=dist.ReduceOp.AVG, group=self.pg)
                             self._record_grad_reads(comm)
                         upd.wait_stream(comm)
-                start = end = None
-                if self.trace is not None:
-                    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    start.record(upd)
-                if len(segs[r]):
-                    if p2p:
-                        self.kernels.multi_step_replicated(upd, segs[r], deltas, self.max_ctas, g_scale)
-                    else:
-                        self.kernels.multi_step(upd, segs[r], self.max_ctas, g_scale)
-                if end is not None:
-                    end.record(upd)
-                    self.trace.append((start, end))
+                self._launch_round(r, target, g_scale)
                 if host_out is not None:
                     d2h.wait_stream(upd)
                     with torch.cuda.stream(d2h):
                         host_out[r * L.chunk:(r + 1) * L.chunk].copy_(
-                            weights[slice(*L.rank_range(r, self.rank))], non_blocking=True)
-                if comm is not None and not p2p:
-                    comm.wait_stream(upd)
-                    with torch.cuda.stream(comm):
-                        out = weights[slice(*L.round_range(r))]
-                        mine = weights[slice(*L.rank_range(r, self.rank))]
-                        dist.all_gather_into_tensor(out, mine, group=self.pg)
-        if p2p:
-            self._barrier(upd)       # every peer's stores into this rank's weights have landed
+                            target[0][slice(*L.rank_range(r, self.rank))], non_blocking=True)
+        self._finish_update(cur, delayed)
+        if h2d is not None:
+            cur.wait_stream(h2d)
+            cur.wait_stream(d2h)
+
+    def _target(self, delayed: bool):
+        """(weight buffer, per-round segments, peer deltas) this step's update writes: the weights, or with
+        delayed updates the second buffer."""
+        if delayed:
+            return self._shadow, self._shadow_segs, self._shadow_deltas
+        return self.flat_weights, self._segs, self._peer_deltas
+
+    def _launch_round(self, r: int, target, g_scale: torch.Tensor | None) -> None:
+        """Round ``r``'s update kernel on the update stream (with the fused all-gather, its peer stores), then
+        -- all-gathered by NCCL -- that round's all-gather on the comm stream."""
+        weights, segs, deltas = target
+        upd, comm = self._update_stream, self._comm_stream
+        start = end = None
+        if self.trace is not None:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(upd)
+        if len(segs[r]):
+            if self._peer_deltas is not None:
+                self.kernels.multi_step_replicated(upd, segs[r], deltas, self.max_ctas, g_scale)
+            else:
+                self.kernels.multi_step(upd, segs[r], self.max_ctas, g_scale)
+        if end is not None:
+            end.record(upd)
+            self.trace.append((start, end))
+        if comm is not None and self._peer_deltas is None:
+            L = self.layout
+            comm.wait_stream(upd)
+            with torch.cuda.stream(comm):
+                dist.all_gather_into_tensor(weights[slice(*L.round_range(r))],
+                                            weights[slice(*L.rank_range(r, self.rank))], group=self.pg)
+
+    def _finish_update(self, cur, delayed: bool) -> None:
+        """After the last round: every peer's stores have landed (fused all-gather), the step is counted, and
+        -- unless the update is delayed -- the caller's stream is ordered after the update and gathers."""
+        if self._peer_deltas is not None:
+            self._barrier(self._update_stream)   # every peer's stores into this rank's weights have landed
         self._steps_done += 1
         self._grads_read, self._grads_read_now = self._grads_read_now, None
         if delayed:
             # the update overlaps whatever the caller runs next; the next step (or flush) makes it the weights
             self._delay_owed = True
         else:
-            cur.wait_stream(upd)
-            if comm is not None:
-                cur.wait_stream(comm)
-        if h2d is not None:
-            cur.wait_stream(h2d)
-            cur.wait_stream(d2h)
+            cur.wait_stream(self._update_stream)
+            if self._comm_stream is not None:
+                cur.wait_stream(self._comm_stream)
+
+    # ------------------------------------------------------------------ updates during backward
+
+    def _backward_update_round(self, r: int) -> None:
+        """Hook mode: update round ``r`` (and all-gather it) as soon as its reduce-scatter is enqueued, while
+        backward goes on.  No barrier is needed first: a rank's reduce-scatter of round ``r`` completes only after
+        every rank has issued its own, which each issues after its backward has finished with round ``r``'s
+        weights -- so no peer still reads the weights these stores overwrite.  The first round of a step also
+        starts the step (step count, group hyperparameters)."""
+        if not self._rounds_updated:
+            self.kernels.check_status("ZeroAdamBridge backward update")
+            self._refresh()
+        upd, comm = self._update_stream, self._comm_stream
+        upd.wait_stream(comm if comm is not None else torch.cuda.current_stream(self.device))
+        with torch.cuda.device(self.device):
+            self._launch_round(r, self._target(False), None)
+        self._rounds_updated.add(r)
+
+    def _updates_in_backward(self) -> bool:
+        return self._hooked and self._update_in_backward and not self._delayed() and not self._delay_owed
 
     # ------------------------------------------------------------------ inspection
 

@@ -410,15 +410,22 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
         model = Decoder().to(torch.bfloat16)
     n_params = sum(p.numel() for p in model.parameters())
     opt = ZeroAdamBridge(list(model.parameters()), lr=2e-5, precision="bf16", rounds=args.rounds,
-                         gather=args.gather, delay_updates=args.delay).attach_hooks(model)
+                         gather=args.gather, delay_updates=args.delay, max_ctas=args.max_ctas)
+    opt.attach_hooks(model, update_in_backward=not args.update_at_step)
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     tokens = torch.randint(0, vocab, (batch, seq + 1), device=dev, generator=gen)
+    marks = []   # (backward's GPU work done, step done) events of every timed step
 
     def step():
         logits = model(tokens[:, :-1])
         loss = F.cross_entropy(logits.float().reshape(-1, vocab), tokens[:, 1:].reshape(-1))
         loss.backward()
+        b = torch.cuda.Event(enable_timing=True)
+        b.record(torch.cuda.current_stream(dev))
         opt.step()
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(torch.cuda.current_stream(dev))
+        marks.append((b, e))
         return loss
 
     for _ in range(args.warmup):
@@ -428,6 +435,7 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.barrier()
     launches0 = kern.launch_count()
     opt.trace = []
+    marks.clear()
     cur = torch.cuda.current_stream(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
@@ -440,11 +448,12 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.barrier()
     ms = t0.elapsed_time(t1) / args.steps
     upd_ms = sum(a.elapsed_time(b) for a, b in opt.trace) / args.steps
+    exposed_ms = sum(b.elapsed_time(e) for b, e in marks) / args.steps
     opt.trace = None
-    t = torch.tensor([ms, upd_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, upd_ms, exposed_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, upd_ms = t.tolist()
+    ms, upd_ms, exposed_ms = t.tolist()
     loss_host = float(loss.detach().float().item())
     if rank != 0:
         return None
@@ -458,7 +467,13 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
                        "hooks": True, "delay_updates": args.delay, "parallelism": f"zero1-dp{world}",
                        "rounds": opt.layout.rounds,
                        "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None},
-            "update_kernels_ms": round(upd_ms, 3), "loss": round(loss_host, 4),
+            "update_kernels_ms": round(upd_ms, 3),
+            "exposed_update_ms": round(exposed_ms, 3),
+            "exposed_basis": "per step, from the end of backward's GPU work (an event after loss.backward()) to the "
+                             "end of opt.step() on the compute stream: the part of the update and all-gather the "
+                             "step waits for; max over ranks",
+            "update_in_backward": not args.update_at_step and not args.delay,
+            "loss": round(loss_host, 4),
             "gpu_launches": kern.launch_count() - launches0, "clocks": clocks.summary()}
     return line
 
@@ -828,6 +843,8 @@ def main() -> int:
                     help="clip_grad_norm_ to this max norm before every step (norm kernels + scaled update)")
     ap.add_argument("--delay", action="store_true",
                     help="--workload train: delayed updates (each update overlaps the next forward)")
+    ap.add_argument("--update-at-step", action="store_true",
+                    help="--workload train: the hooks only reduce-scatter; every round is updated at step()")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-variant-seconds", type=float, default=3.0,

@@ -301,7 +301,9 @@ def _hooks_vs_step(rank, world, device, gather, clip, steps=3):
     kw = dict(lr=2e-3, precision="bf16", seed=3, rounds=3)
     if gather is not None:
         kw["gather"] = gather
-    oa = ZeroAdamBridge(list(ma.parameters()), **kw).attach_hooks(ma)
+    # with clipping, the hooks only reduce-scatter (the clip needs every gradient before any update); without,
+    # each round is also updated during backward
+    oa = ZeroAdamBridge(list(ma.parameters()), **kw).attach_hooks(ma, update_in_backward=clip is None)
     ob = ZeroAdamBridge(list(mb.parameters()), **kw)
     for step in range(1, steps + 1):
         for model, opt in ((ma, oa), (mb, ob)):
@@ -318,6 +320,29 @@ def _hooks_vs_step(rank, world, device, gather, clip, steps=3):
 def test_zero_hooks_equal_step_world1(clip):
     got, want = _hooks_vs_step(0, 1, "cuda", None, clip)
     assert all(torch.equal(a, b) for a, b in zip(got, want))
+
+
+@pytest.mark.parametrize("in_backward", [True, False])
+def test_zero_hooks_update_during_backward(in_backward):
+    """With update_in_backward every round's update is enqueued by the hooks (the weights change before step()
+    on the GPU timeline); step() only ends the step.  Either way the weights equal step()'s."""
+    ma, mb = _mlp_pair("cuda")
+    oa = ZeroAdamBridge(list(ma.parameters()), lr=2e-3, precision="bf16", seed=3, rounds=3)
+    oa.attach_hooks(ma, update_in_backward=in_backward)
+    ob = ZeroAdamBridge(list(mb.parameters()), lr=2e-3, precision="bf16", seed=3, rounds=3)
+    for step in range(1, 4):
+        _mlp_loss(ma, step, 0, "cuda").backward()
+        assert len(oa._rounds_updated) == (3 if in_backward else 0)
+        oa.step()
+        assert not oa._rounds_updated
+        _mlp_loss(mb, step, 0, "cuda").backward()
+        ob.step()
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, b) for a, b in zip(ma.parameters(), mb.parameters()))
+    if in_backward:
+        _mlp_loss(ma, 9, 0, "cuda").backward()
+        with pytest.raises(RuntimeError, match="update_in_backward=False"):
+            oa.clip_grad_norm_(1.0)
 
 
 def test_zero_hooks_reject_a_second_gradient():
