@@ -478,6 +478,80 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
     return line
 
 
+# --------------------------------------------------------------------------- state conversion
+
+CONVERT_BYTES = {"fp32": 4.0, "bf16": 2.0, "fp8": 1.0 + 4.0 / 128, "fp24": 3.0}
+
+
+def convert_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """--workload convert: libabx's state-format conversion kernel (abx_convert) re-encoding the second moment of
+    the 7B parameter set -- 6,738,415,616 values -- from ``--convert-from`` to ``--precision`` (what
+    ``set_precision`` does to every moment), one launch per tensor, CUDA events.  Algorithmic bytes: the source
+    read plus the destination written (fp32 4, bf16 2, fp8 1 + 4/128 per value)."""
+    import torch
+
+    from adambridge_b200 import native
+    from adambridge_b200.precision import StateBuffer
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    kern = native.load()
+    dims = dict(LLAMA7B)
+    if args.layers is not None:
+        dims["layers"] = args.layers
+    if args.vocab is not None:
+        dims["vocab"] = args.vocab
+    sizes = [numel(s) for s in llama_shapes(**dims)]
+    total = sum(sizes)
+    src_fmt, dst_fmt = args.convert_from, args.precision
+    gen = torch.Generator(device=dev).manual_seed(77)
+    srcs, dsts = [], []
+    with torch.no_grad():
+        for n in sizes:
+            v = torch.empty(n, device=dev).exponential_(generator=gen).mul_(1e-6)   # v >= 0, like a second moment
+            srcs.append(StateBuffer.converted(v, src_fmt, "v", dev))
+            del v
+            dsts.append(StateBuffer.allocate(dst_fmt, "v", n, dev))
+    cur = torch.cuda.current_stream(dev)
+
+    def once():
+        for s, d in zip(srcs, dsts):
+            d.assign(s)
+
+    for _ in range(args.warmup):
+        once()
+    torch.cuda.synchronize()
+    launches0 = kern.launch_count()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        a.record(cur)
+        for _ in range(args.steps):
+            once()
+        b.record(cur)
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    launches = kern.launch_count() - launches0
+    if rank != 0:
+        return None
+    bpv = CONVERT_BYTES[src_fmt] + CONVERT_BYTES[dst_fmt]
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = bpv * total / (ms / 1e3) / 1e9
+    return {"metric": f"state conversion Gvalues/s ({src_fmt} -> {dst_fmt} moments)",
+            "value": round(total / (ms / 1e3) / 1e9, 3), "unit": "Gvalues/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"llama7b-second-moment-{src_fmt}-to-{dst_fmt}", "values": total,
+                       "tensors": len(sizes), "l2": "no flush: %.1f GB per step >> 126 MB L2" % (bpv * total / 1e9)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "basis": f"{bpv:g} B/value (source read + destination written) x {total:,} values / "
+                                  "conversion time (CUDA events), one abx_convert launch per tensor; peak = "
+                                  + ("MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks
+                                     else "6650 GB/s (of fallback)")},
+            "gpu_launches": launches, "clocks": clocks.summary()}
+
+
 # --------------------------------------------------------------------------- multi-GPU checks
 
 def sharded_parity(args, world: int, rank: int, dev) -> dict:
@@ -828,8 +902,11 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="abx", choices=["abx", "reference", "reference-gpu"])
-    ap.add_argument("--workload", default="update", choices=["update", "train"],
-                    help="update: the fused optimizer step (the headline); train: config 5's training step")
+    ap.add_argument("--workload", default="update", choices=["update", "train", "convert"],
+                    help="update: the fused optimizer step (the headline); train: config 5's training step; "
+                         "convert: the state-format conversion kernel on the 7B set's second moment")
+    ap.add_argument("--convert-from", default="fp32", choices=["fp32", "bf16", "fp8"],
+                    help="--workload convert: the source format (the destination is --precision)")
     ap.add_argument("--algorithm", default="adamw", choices=["adamw", "lion"])
     ap.add_argument("--precision", default="bf16", choices=["fp32", "bf16", "fp8"])
     ap.add_argument("--rounds", type=int, default=8,
@@ -885,6 +962,8 @@ def main() -> int:
     try:
         if args.workload == "train":
             line = train_arm(args, rank, world, local_rank)
+        elif args.workload == "convert":
+            line = convert_arm(args, rank, world, local_rank)
         else:
             line = gpu_arm(args, rank, world, local_rank)
     finally:
