@@ -259,22 +259,12 @@ def reference_arm(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def reference_gpu_arm(args, rank: int) -> None:
-    """--impl reference-gpu: the reference's only GPU update, its gpu_state_budget path
-    (adambridge/optimizer.py:364-430, _step_gpu), on the same 7B parameter set: FP32 master weights and
-    moments on the GPU, each bf16 gradient converted with grad.to(float32), torch.optim.AdamW(fused=True),
-    then torch._foreach_copy_ of the masters into the bf16 weights.  Rank 0 only; for context beside the
-    reference's CPU arm, not part of the driver's contract."""
-    if rank != 0:
-        return
+def torch_fused_adamw_rate(dims: dict, steps: int, warmup: int, dev) -> dict:
+    """The reference's only GPU update, its gpu_state_budget path (adambridge/optimizer.py:364-430, _step_gpu), on
+    the parameter set ``dims``: FP32 master weights and moments on the GPU, each bf16 gradient converted with
+    grad.to(float32), torch.optim.AdamW(fused=True), then torch._foreach_copy_ of the masters into the bf16
+    weights.  CUDA events; returns the rate, the time and the roofline of the bytes that path moves."""
     import torch
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    dims = dict(LLAMA7B)
-    if args.layers is not None:
-        dims["layers"] = args.layers
-    if args.vocab is not None:
-        dims["vocab"] = args.vocab
     shapes = llama_shapes(**dims)
     n_params = sum(numel(sh) for sh in shapes)
     gen = torch.Generator(device=dev).manual_seed(1234)
@@ -295,34 +285,57 @@ def reference_gpu_arm(args, rank: int) -> None:
         for mp in masters:
             mp.grad = None
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
-    torch.cuda.synchronize()
+    torch.cuda.synchronize(dev)
     cur = torch.cuda.current_stream(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clocks:
+    with ClockSampler(dev.index or 0) as clocks:
         t0.record(cur)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         t1.record(cur)
-        torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1) / args.steps
+        torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    del inner, masters, grads, weights
+    torch.cuda.empty_cache()
     # bytes the path moves: grad bf16 read + fp32 write, fused AdamW (p, g, m, v read; p, m, v written, fp32),
     # master read + bf16 weight write
     bpp = 2 + 4 + 7 * 4 + 4 + 2
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("hbm_gbs", 6650.0)
     achieved = bpp * n_params / (ms / 1e3) / 1e9
-    line = {"impl": "reference-gpu", "metric": "fused step Gparams/s (7B, the reference's GPU update)",
-            "value": round(n_params / (ms / 1e3) / 1e9, 4), "unit": "Gparams/s", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "llama7b-adamw-fp32-state-torch-fused (gpu_state_budget path)",
-                       "params": n_params, "tensors": len(shapes)},
+    return {"value": round(n_params / (ms / 1e3) / 1e9, 4), "unit": "Gparams/s", "ms_per_step": round(ms, 3),
+            "steps": steps, "params": n_params,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
                          "basis": f"{bpp} B/param moved by grad.to(fp32) + fused AdamW + _foreach_copy_"},
-            "clocks": clocks.summary()}
+            "clocks": clocks.summary(),
+            "path": "the reference's gpu_state_budget update: fp32 state on the GPU, grad.to(float32), "
+                    "torch.optim.AdamW(fused=True), torch._foreach_copy_ into the bf16 weights"}
+
+
+def reference_gpu_arm(args, rank: int) -> None:
+    """--impl reference-gpu: torch_fused_adamw_rate on the 7B set as its own line (rank 0 only).  The default
+    N = 1 run of the repo's arm also reports it, as ``reference_gpu_update``."""
+    if rank != 0:
+        return
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dims = dict(LLAMA7B)
+    if args.layers is not None:
+        dims["layers"] = args.layers
+    if args.vocab is not None:
+        dims["vocab"] = args.vocab
+    r = torch_fused_adamw_rate(dims, args.steps, args.warmup, dev)
+    line = {"impl": "reference-gpu", "metric": "fused step Gparams/s (7B, the reference's GPU update)",
+            "value": r["value"], "unit": "Gparams/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "llama7b-adamw-fp32-state-torch-fused (gpu_state_budget path)",
+                       "params": r["params"]},
+            "roofline": r["roofline"], "clocks": r["clocks"]}
     print(json.dumps(line), flush=True)
 
 
@@ -828,6 +841,12 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
     del opt
     torch.cuda.empty_cache()
     parity = None if args.no_parity else sharded_parity(args, world, rank, dev)
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu and (algo, prec) == ("adamw", "bf16"):
+        # the reference's own GPU update on the same parameter set, with this run's state freed first
+        del params
+        torch.cuda.empty_cache()
+        ref_gpu = torch_fused_adamw_rate(dims, max(2, min(args.steps, 5)), 2, dev)
 
     if rank != 0:
         return None
@@ -891,6 +910,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
                                             else "HBM traffic of the update kernel")}
     if parity is not None:
         line["parity"] = parity
+    if ref_gpu is not None:
+        line["reference_gpu_update"] = ref_gpu
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_block(args)
     return line
@@ -929,6 +950,8 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the sharded-vs-unsharded check after timing")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="N = 1: skip timing the reference's own GPU update (torch fused AdamW) after the step")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "abx":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
