@@ -140,6 +140,60 @@ __device__ __forceinline__ float warp_absmax_nan(const float (&a)[4])
     return __any_sync(0xffffffffU, nan) ? __uint_as_float(0x7fc00000U) : u2f(m);
 }
 
+// The FP8 codes of a warp's 128-value block (4 per lane; values past the end are the padding, 0) and its scale
+// (FP8Store.write: a second moment is kept as sqrt(max(v, 0)); scale = absmax / fmax, 1 for an all-zero or NaN
+// block; values divided, clamped to +-fmax and cast).  A NaN passes through all of that on the host with its
+// sign and becomes code 0x7f | sign (torch's float8 casts); it is carried past the arithmetic here.
+__device__ __forceinline__ uint32_t fp8_block_codes(float (&x)[4], bool v, float& scale)
+{
+    const float fmax = v ? 57344.0f : 448.0f;
+    if (v) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (x[k] == x[k]) x[k] = __fsqrt_rn(x[k] < 0.0f ? 0.0f : x[k]);
+    }
+    const float amax = warp_absmax_nan(x);
+    scale = amax > 0.0f ? __fdiv_rn(amax, fmax) : 1.0f;
+    uint32_t w = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t code;
+        if (x[k] != x[k]) {
+            code = 0x7fU | ((f2u(x[k]) >> 24) & 0x80U);
+        } else {
+            float q = __fdiv_rn(x[k], scale);
+            if (q != q) {
+                code = 0xffU;   // inf / inf (an infinite value, so an infinite scale): the host's
+                                // invalid-operation NaN has its sign bit set
+            } else {
+                q = q < -fmax ? -fmax : (q > fmax ? fmax : q);
+                code = fp8_code_of(q, v);
+            }
+        }
+        w |= code << (8 * k);
+    }
+    return w;
+}
+
+// One value into a non-FP8 destination.
+__device__ __forceinline__ void store_value(const View& d, int64_t i, float x)
+{
+    switch (d.dtype) {
+    case ABX_DT_F32:
+        static_cast<float*>(d.values)[i] = x;
+        break;
+    case ABX_DT_BF16:
+        static_cast<uint16_t*>(d.values)[i] = (uint16_t)bf16_bits_of(x);
+        break;
+    default: {   // ABX_DT_F24: nearest-even to the top 24 bits; NaN quieted and kept whole
+        const uint32_t b = abx::f24_bits(f2u(x), false, 0U);
+        static_cast<uint16_t*>(d.values)[i] = (uint16_t)(b >> 16);
+        static_cast<uint8_t*>(d.aux)[i] = (uint8_t)(b >> 8);
+    }
+    }
+}
+
+// Any source (any FP8 block, any alignment), any destination: one value at a time.
 __global__ void __launch_bounds__(kThreads) convert_kernel(const __grid_constant__ ConvArgs a)
 {
     const int lane = threadIdx.x & 31;
@@ -151,59 +205,120 @@ __global__ void __launch_bounds__(kThreads) convert_kernel(const __grid_constant
         for (int k = 0; k < 4; ++k) x[k] = i0 + k < a.n ? load_value(a.src, i0 + k) : 0.0f;   // padding is 0
         const View& d = a.dst;
         if (d.dtype == ABX_DT_FP8) {
-            // FP8Store.write: a second moment is kept as sqrt(max(v, 0)); the block's scale is absmax / fmax
-            // (1 for an all-zero or NaN block); values are divided by it, clamped to +-fmax and cast.
-            // A NaN passes through all of that on the host with its sign and becomes code 0x7f | sign (torch's
-            // float8 casts); it is carried past the arithmetic here.
-            const bool v = d.v_role != 0;
-            const float fmax = v ? 57344.0f : 448.0f;
-            if (v) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (x[k] == x[k]) x[k] = __fsqrt_rn(x[k] < 0.0f ? 0.0f : x[k]);
-            }
-            const float amax = warp_absmax_nan(x);
-            const float scale = amax > 0.0f ? __fdiv_rn(amax, fmax) : 1.0f;
-            uint32_t w = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                uint32_t code;
-                if (x[k] != x[k]) {
-                    code = 0x7fU | ((f2u(x[k]) >> 24) & 0x80U);
-                } else {
-                    float q = __fdiv_rn(x[k], scale);
-                    if (q != q) {
-                        code = 0xffU;   // inf / inf (an infinite value, so an infinite scale): the host's
-                                        // invalid-operation NaN has its sign bit set
-                    } else {
-                        q = q < -fmax ? -fmax : (q > fmax ? fmax : q);
-                        code = fp8_code_of(q, v);
-                    }
-                }
-                w |= code << (8 * k);
-            }
+            float scale;
+            const uint32_t w = fp8_block_codes(x, d.v_role != 0, scale);
             *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(d.values) + i0) = w;   // whole padded block
             if (lane == 0) static_cast<float*>(d.aux)[blk] = scale;
             continue;
         }
 #pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (i0 + k < a.n) store_value(d, i0 + k, x[k]);
+    }
+}
+
+// ---- vector path: one kernel per (source, destination) format pair -------------------------------
+// Every buffer aligned for 4-value vectors and an FP8 source in 128-value blocks (so a warp's block is the
+// source's block and its scale one load): each lane moves its 4 values with one load and one store per plane.
+
+template <int DT>
+__device__ __forceinline__ void load4(const View& s, int64_t i0, int64_t blk, float (&x)[4])
+{
+    if constexpr (DT == ABX_DT_F32) {
+        const float4 q = *reinterpret_cast<const float4*>(static_cast<const float*>(s.values) + i0);
+        x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+    } else if constexpr (DT == ABX_DT_BF16) {
+        const uint2 q = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(s.values) + i0);
+        x[0] = u2f(q.x << 16); x[1] = u2f(q.x & 0xffff0000U); x[2] = u2f(q.y << 16); x[3] = u2f(q.y & 0xffff0000U);
+    } else if constexpr (DT == ABX_DT_F24) {
+        const uint2 h = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(s.values) + i0);
+        const uint32_t lo = *reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(s.aux) + i0);
+        x[0] = u2f((h.x << 16) | ((lo & 0xffU) << 8));
+        x[1] = u2f((h.x & 0xffff0000U) | (lo & 0xff00U));
+        x[2] = u2f((h.y << 16) | ((lo >> 8) & 0xff00U));
+        x[3] = u2f((h.y & 0xffff0000U) | ((lo >> 16) & 0xff00U));
+    } else {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(s.values) + i0);
+        const float sc = static_cast<const float*>(s.aux)[blk];
+        const bool v = s.v_role != 0;
+#pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int64_t i = i0 + k;
-            if (i >= a.n) break;
-            switch (d.dtype) {
-            case ABX_DT_F32:
-                static_cast<float*>(d.values)[i] = x[k];
-                break;
-            case ABX_DT_BF16:
-                static_cast<uint16_t*>(d.values)[i] = (uint16_t)bf16_bits_of(x[k]);
-                break;
-            default: {   // ABX_DT_F24: nearest-even to the top 24 bits; NaN quieted and kept whole
-                const uint32_t b = abx::f24_bits(f2u(x[k]), false, 0U);
-                static_cast<uint16_t*>(d.values)[i] = (uint16_t)(b >> 16);
-                static_cast<uint8_t*>(d.aux)[i] = (uint8_t)(b >> 8);
-            }
-            }
+            const uint32_t c = (w >> (8 * k)) & 0xffU;
+            const uint32_t nan = fp8_nan_bits(c, v);
+            float y = __fmul_rn(fp8_value(c, v), sc);
+            if (y != y) y = sc != sc ? u2f(f2u(sc) | 0x00400000U) : u2f(0xffc00000U);   // see load_value
+            else if (v) y = __fmul_rn(y, y);
+            x[k] = nan ? u2f(nan) : y;
         }
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ void store4(const View& d, int64_t i0, const float (&x)[4])
+{
+    if constexpr (DT == ABX_DT_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(d.values) + i0) = make_float4(x[0], x[1], x[2], x[3]);
+    } else if constexpr (DT == ABX_DT_BF16) {
+        const uint32_t b0 = bf16_bits_of(x[0]), b1 = bf16_bits_of(x[1]), b2 = bf16_bits_of(x[2]), b3 = bf16_bits_of(x[3]);
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(d.values) + i0) = make_uint2(b0 | (b1 << 16), b2 | (b3 << 16));
+    } else {   // ABX_DT_F24
+        uint32_t b[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) b[k] = abx::f24_bits(f2u(x[k]), false, 0U);
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(d.values) + i0) =
+            make_uint2((b[0] >> 16) | (b[1] & 0xffff0000U), (b[2] >> 16) | (b[3] & 0xffff0000U));
+        *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(d.aux) + i0) =
+            ((b[0] >> 8) & 0xffU) | (b[1] & 0xff00U) | ((b[2] << 8) & 0xff0000U) | ((b[3] << 16) & 0xff000000U);
+    }
+}
+
+template <int SRC, int DST>
+__global__ void __launch_bounds__(kThreads) convert_vec_kernel(const __grid_constant__ ConvArgs a)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * kWarps;
+    for (int64_t blk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); blk < a.nblocks; blk += warps) {
+        const int64_t i0 = blk * kBlock + lane * 4;
+        const bool whole = i0 + 4 <= a.n;
+        float x[4];
+        if (whole) {
+            load4<SRC>(a.src, i0, blk, x);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[k] = i0 + k < a.n ? load_value(a.src, i0 + k) : 0.0f;
+        }
+        if constexpr (DST == ABX_DT_FP8) {
+            float scale;
+            const uint32_t w = fp8_block_codes(x, a.dst.v_role != 0, scale);
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(a.dst.values) + i0) = w;
+            if (lane == 0) static_cast<float*>(a.dst.aux)[blk] = scale;
+        } else if (whole) {
+            store4<DST>(a.dst, i0, x);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (i0 + k < a.n) store_value(a.dst, i0 + k, x[k]);
+        }
+    }
+}
+
+using VecKernel = void (*)(ConvArgs);
+constexpr int kFormats = 4;   // ABX_DT_F32, _BF16, _FP8, _F24 are codes 1..4
+
+#define ABX_VEC_ROW(S) convert_vec_kernel<S, ABX_DT_F32>, convert_vec_kernel<S, ABX_DT_BF16>, \
+                       convert_vec_kernel<S, ABX_DT_FP8>, convert_vec_kernel<S, ABX_DT_F24>
+const VecKernel kVecKernels[kFormats][kFormats] = {{ABX_VEC_ROW(ABX_DT_F32)}, {ABX_VEC_ROW(ABX_DT_BF16)},
+                                                   {ABX_VEC_ROW(ABX_DT_FP8)}, {ABX_VEC_ROW(ABX_DT_F24)}};
+
+// Whether a buffer's planes allow 4-value vector accesses (and, for an FP8 source, are in 128-value blocks).
+bool vector_ready(const abx_state* s)
+{
+    const uintptr_t v = reinterpret_cast<uintptr_t>(s->values), x = reinterpret_cast<uintptr_t>(s->aux);
+    switch (s->dtype) {
+    case ABX_DT_F32: return v % 16 == 0;
+    case ABX_DT_BF16: return v % 8 == 0;
+    case ABX_DT_F24: return v % 8 == 0 && x % 4 == 0;
+    default: return v % 4 == 0 && s->block == kBlock;
     }
 }
 
@@ -249,7 +364,11 @@ ABX_API int abx_convert(void* stream, const abx_state* src, const abx_state* dst
     if (e != cudaSuccess) return abx::set_error("abx_convert: querying the device", e);
     const int64_t want = (a.nblocks + kWarps - 1) / kWarps;
     const int grid = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
-    convert_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (vector_ready(src) && vector_ready(dst))
+        kVecKernels[src->dtype - 1][dst->dtype - 1]<<<grid, kThreads, 0, st>>>(a);
+    else
+        convert_kernel<<<grid, kThreads, 0, st>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return abx::set_error("abx_convert launch", e);
     abx::g_launches.fetch_add(1, std::memory_order_relaxed);

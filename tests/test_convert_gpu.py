@@ -105,15 +105,43 @@ def test_every_pair_of_formats_matches_the_checker(src, dst, n):
         want = src_planes        # the same layout: the planes are copied as they are
     else:
         want = C.encode(dst[0], C.decode(src[0], src_planes, n, src[1]), dst[1])
+    out = StateBuffer.converted(_on_device(src, n, src_planes, misalign=False), dst[0], dst[1], DEV)
+    _assert_planes(out, want)
+
+
+def _on_device(fmt_role, n, planes, misalign: bool) -> StateBuffer:
+    """The planes as device tensors; ``misalign`` starts every plane one element into its allocation, so no
+    plane is aligned for vector accesses (the conversion's one-value-at-a-time kernel)."""
     tensors = {}
-    for k, a in src_planes.items():
-        t = torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a).to(DEV)
-        tensors[k] = t
-    buf = StateBuffer(src[0], src[1], n, tensors)
-    out = StateBuffer.converted(buf, dst[0], dst[1], DEV)
+    for k, a in planes.items():
+        t = torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a)
+        if misalign and k != "scale":
+            tensors[k] = torch.cat([t[:1], t]).to(DEV)[1:]   # one element into its allocation
+        else:
+            tensors[k] = t.to(DEV)
+    return StateBuffer(fmt_role[0], fmt_role[1], n, tensors)
+
+
+def _assert_planes(out: StateBuffer, want: dict) -> None:
     for k, a in want.items():
         got = as_np(out.planes[k])
         if a.dtype == np.float32:
             assert same_floats(got, a), k
         else:
             assert np.array_equal(got.view(a.dtype), a), k
+
+
+@pytest.mark.parametrize("n", [129, 100_003])
+@pytest.mark.parametrize("src", FORMATS)
+@pytest.mark.parametrize("dst", [f for f in FORMATS if f[0] != "fp8"] + [("fp8", "m")])
+def test_unaligned_buffers_take_the_scalar_kernel(src, dst, n):
+    """Sources that start one element into their allocation (no vector access possible) convert to the same bits
+    as the checker gives."""
+    if src[0] == dst[0] and src[0] != "fp8":
+        return   # same layout: a plane copy, no kernel
+    rng = np.random.default_rng(n + 17)
+    x = np.abs((rng.standard_normal(n) * 10.0 ** rng.uniform(-8, 3, n)).astype(np.float32))
+    src_planes = C.encode(src[0], x, src[1])
+    want = C.encode(dst[0], C.decode(src[0], src_planes, n, src[1]), dst[1])
+    out = StateBuffer.converted(_on_device(src, n, src_planes, misalign=True), dst[0], dst[1], DEV)
+    _assert_planes(out, want)

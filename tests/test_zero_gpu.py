@@ -334,9 +334,11 @@ def test_zero_hooks_update_during_backward(in_backward):
         _mlp_loss(ma, step, 0, "cuda").backward()
         assert len(oa._rounds_updated) == (3 if in_backward else 0)
         oa.step()
+        oa.zero_grad()
         assert not oa._rounds_updated
         _mlp_loss(mb, step, 0, "cuda").backward()
         ob.step()
+        ob.zero_grad()
     torch.cuda.synchronize()
     assert all(torch.equal(a, b) for a, b in zip(ma.parameters(), mb.parameters()))
     if in_backward:
