@@ -153,7 +153,12 @@ __device__ __forceinline__ uint32_t fp8_block_codes(float (&x)[4], bool v, float
             if (x[k] == x[k]) x[k] = __fsqrt_rn(x[k] < 0.0f ? 0.0f : x[k]);
     }
     const float amax = warp_absmax_nan(x);
-    scale = amax > 0.0f ? __fdiv_rn(amax, fmax) : 1.0f;
+    // RN(amax / fmax) and, in the common range of scales, the quotients by Markstein's correction with
+    // RN(1 / scale) -- both correctly rounded, as the update kernel divides by a block scale (abx_device.cuh:
+    // scale_of, fast_scale, div_by_scale); outside that range, IEEE division
+    scale = amax > 0.0f ? (v ? abx::scale_of<false>(amax) : abx::scale_of<true>(amax)) : 1.0f;
+    const bool fast = abx::fast_scale(scale);
+    const float y = fast ? __frcp_rn(scale) : 0.0f;
     uint32_t w = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -161,7 +166,7 @@ __device__ __forceinline__ uint32_t fp8_block_codes(float (&x)[4], bool v, float
         if (x[k] != x[k]) {
             code = 0x7fU | ((f2u(x[k]) >> 24) & 0x80U);
         } else {
-            float q = __fdiv_rn(x[k], scale);
+            float q = fast ? abx::div_by_scale(x[k], scale, y) : __fdiv_rn(x[k], scale);
             if (q != q) {
                 code = 0xffU;   // inf / inf (an infinite value, so an infinite scale): the host's
                                 // invalid-operation NaN has its sign bit set
