@@ -125,8 +125,9 @@ __device__ __forceinline__ uint32_t fp8_code_of(float q, bool e5m2)
     return (uint32_t)c2 & 0xffU;
 }
 
-// Largest of four magnitudes over the warp, NaN if any value of the warp is NaN (torch's amax propagates NaN).
-__device__ __forceinline__ float warp_absmax_nan(const float (&a)[4])
+// Largest of four magnitudes over the warp, ignoring NaNs, and whether any value of the warp is NaN (torch's
+// amax propagates NaN: the caller then treats the block maximum as NaN).
+__device__ __forceinline__ float warp_absmax(const float (&a)[4], bool& any_nan)
 {
     bool nan = false;
     uint32_t m = 0;
@@ -136,14 +137,10 @@ __device__ __forceinline__ float warp_absmax_nan(const float (&a)[4])
         const uint32_t b = f2u(a[k]) & 0x7fffffffU;   // |a|: non-negative floats order like their bits
         m = (a[k] == a[k] && b > m) ? b : m;
     }
-    m = __reduce_max_sync(0xffffffffU, m);
-    return __any_sync(0xffffffffU, nan) ? __uint_as_float(0x7fc00000U) : u2f(m);
+    any_nan = __any_sync(0xffffffffU, nan);
+    return u2f(__reduce_max_sync(0xffffffffU, m));
 }
 
-// The FP8 codes of a warp's 128-value block (4 per lane; values past the end are the padding, 0) and its scale
-// (FP8Store.write: a second moment is kept as sqrt(max(v, 0)); scale = absmax / fmax, 1 for an all-zero or NaN
-// block; values divided, clamped to +-fmax and cast).  A NaN passes through all of that on the host with its
-// sign and becomes code 0x7f | sign (torch's float8 casts); it is carried past the arithmetic here.
 __device__ __forceinline__ uint32_t fp8_block_codes(float (&x)[4], bool v, float& scale)
 {
     const float fmax = v ? 57344.0f : 448.0f;
@@ -152,13 +149,35 @@ __device__ __forceinline__ uint32_t fp8_block_codes(float (&x)[4], bool v, float
         for (int k = 0; k < 4; ++k)
             if (x[k] == x[k]) x[k] = __fsqrt_rn(x[k] < 0.0f ? 0.0f : x[k]);
     }
-    const float amax = warp_absmax_nan(x);
-    // RN(amax / fmax) and, in the common range of scales, the quotients by Markstein's correction with
-    // RN(1 / scale) -- both correctly rounded, as the update kernel divides by a block scale (abx_device.cuh:
-    // scale_of, fast_scale, div_by_scale); outside that range, IEEE division
+    bool any_nan;
+    const float amax_finite = warp_absmax(x, any_nan);
+    const float amax = any_nan ? __uint_as_float(0x7fc00000U) : amax_finite;
+    // RN(amax / fmax): the constant reciprocal with Markstein's correction (abx_device.cuh: scale_of)
     scale = amax > 0.0f ? (v ? abx::scale_of<false>(amax) : abx::scale_of<true>(amax)) : 1.0f;
-    const bool fast = abx::fast_scale(scale);
-    const float y = fast ? __frcp_rn(scale) : 0.0f;
+    if (__builtin_expect(!any_nan && abx::fast_scale(scale), 1)) {
+        // Every value finite and the scale in Markstein's range: the correctly rounded quotients pairwise
+        // (abx_device.cuh: div2, valid there for |x| >= 2^-100; smaller quotients encode to a zero code
+        // whatever their last bits), the sign put back (a zero keeps its sign), then two values per
+        // conversion.  cvt.satfinite saturates at the format's largest finite value, which is what the
+        // reference's clamp to +-fmax before its nearest-even cast gives.
+        const float y = __frcp_rn(scale);
+        const abx::f2x Y = abx::pk2(y, y), NS = abx::pk2(-scale, -scale);
+        float q[4];
+        abx::up2(abx::div2(abx::pk2(x[0], x[1]), Y, NS), q[0], q[1]);
+        abx::up2(abx::div2(abx::pk2(x[2], x[3]), Y, NS), q[2], q[3]);
+        uint16_t c01, c23;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = copysignf(q[k], x[k]);
+        if (v) {
+            asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c01) : "f"(q[1]), "f"(q[0]));
+            asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(q[3]), "f"(q[2]));
+        } else {
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(c01) : "f"(q[1]), "f"(q[0]));
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(c23) : "f"(q[3]), "f"(q[2]));
+        }
+        return (uint32_t)c01 | ((uint32_t)c23 << 16);
+    }
+    // A NaN in the block, or a scale outside Markstein's range (tiny or infinite): value by value, IEEE division.
     uint32_t w = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -166,7 +185,7 @@ __device__ __forceinline__ uint32_t fp8_block_codes(float (&x)[4], bool v, float
         if (x[k] != x[k]) {
             code = 0x7fU | ((f2u(x[k]) >> 24) & 0x80U);
         } else {
-            float q = fast ? abx::div_by_scale(x[k], scale, y) : __fdiv_rn(x[k], scale);
+            float q = __fdiv_rn(x[k], scale);
             if (q != q) {
                 code = 0xffU;   // inf / inf (an infinite value, so an infinite scale): the host's
                                 // invalid-operation NaN has its sign bit set
