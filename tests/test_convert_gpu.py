@@ -145,3 +145,32 @@ def test_unaligned_buffers_take_the_scalar_kernel(src, dst, n):
     want = C.encode(dst[0], C.decode(src[0], src_planes, n, src[1]), dst[1])
     out = StateBuffer.converted(_on_device(src, n, src_planes, misalign=True), dst[0], dst[1], DEV)
     _assert_planes(out, want)
+
+
+@pytest.mark.parametrize("role", ["m", "v"])
+def test_every_bf16_value_into_fp8(role):
+    """All 65,536 bf16 bit patterns (zeros, subnormals, infinities, NaNs of both signs among them), in 512 blocks
+    whose ranges differ, re-encoded as FP8: the kernel's codes and scales are the checker's."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    src_planes = {"data": bits}
+    want = C.encode("fp8", C.decode("bf16", src_planes, bits.size, "m"), role)
+    out = StateBuffer.converted(_on_device(("bf16", "m"), bits.size, src_planes, misalign=False), "fp8", role, DEV)
+    _assert_planes(out, want)
+
+
+@pytest.mark.parametrize("role", ["m", "v"])
+def test_every_fp8_code_decodes(role):
+    """Every code under block scales from 2^-126 to 2^126 (and 0, inf, NaN scales) decodes to the checker's
+    values, NaN signs and the host's 0 x inf NaN included."""
+    scales = np.array([2.0 ** e for e in range(-126, 127, 9)] + [0.0, np.inf, np.nan, 1.0, 3e-45],
+                      np.float32)
+    codes = np.tile(np.arange(256, dtype=np.uint8), 2 * scales.size)     # two blocks of 128 per scale
+    planes = {"q": codes, "scale": np.repeat(scales, 4)}
+    n = codes.size
+    want = C.decode("fp8", planes, n, role)
+    got = StateBuffer("fp8", role, n, {"q": torch.from_numpy(codes).to(DEV),
+                                       "scale": torch.from_numpy(planes["scale"]).to(DEV)}).to_fp32()
+    g = as_np(got)
+    assert same_floats(g, want)
+    nan = np.isnan(want)
+    assert np.array_equal(g[nan].view(np.uint32) >> 31, want[nan].view(np.uint32) >> 31)   # NaN signs
