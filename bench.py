@@ -974,7 +974,9 @@ def main() -> int:
         # NCCL logs its communicators (INFO: ranks, devices, transports) to standard output.  Everything this
         # process writes to standard output from here on goes to standard error instead, so the result line,
         # written to the saved descriptor, is the only line on standard output.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "NONE", "VERSION", "WARN"):
+            os.environ["NCCL_DEBUG"] = "INFO"          # communicator size and transports, on standard error
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT,ENV")
         sys.stdout.flush()
         result_fd = os.dup(1)
         os.dup2(2, 1)
