@@ -247,6 +247,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._clip_coef: torch.Tensor | None = None
         self._norm_state = None
         self._update_in_backward = False
+        self._backward_ctas = max_ctas
         self._rounds_updated: set[int] = set()   # hook mode: rounds this step already updated during backward
 
     # ------------------------------------------------------------------ fused all-gather
@@ -427,8 +428,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     # ------------------------------------------------------------------ gradients reduced during backward
 
-    def attach_hooks(self, model: torch.nn.Module | None = None,
-                     update_in_backward: bool = True) -> "ZeroAdamBridge":
+    def attach_hooks(self, model: torch.nn.Module | None = None, update_in_backward: bool = True,
+                     backward_max_ctas: int | None = None) -> "ZeroAdamBridge":
         """Reduce-scatter the gradients during backward (the data-parallel gradient path) and, with
         ``update_in_backward``, update the weights during backward too.
 
@@ -441,8 +442,21 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         update stream, and ``step()`` only ends the step; otherwise ``step()`` updates every round.  Delayed
         updates and :meth:`clip_grad_norm_` (which needs every gradient before any update) update at ``step()``:
         pass ``update_in_backward=False`` to clip.  The overlap is per round: construct the optimizer with
-        ``rounds`` > 1 for it.  Every parameter must receive exactly one gradient per step."""
+        ``rounds`` > 1 for it.  Every parameter must receive exactly one gradient per step.
+
+        ``backward_max_ctas`` caps the CTAs of the updates run during backward (0: every SM).  By default it is
+        one CTA per SM where the all-gather is fused (world > 1): that update waits on NVLink, and leaving SMs to
+        the backward pass shortens the step (Llama-7B on 8 B200: 288.4 ms per step against 292.4 ms uncapped);
+        on one GPU, where the update is HBM-bound, the constructor's ``max_ctas`` applies."""
         self._update_in_backward = bool(update_in_backward)
+        if backward_max_ctas is not None:
+            if backward_max_ctas < 0:
+                raise ValueError("backward_max_ctas must be >= 0")
+            self._backward_ctas = int(backward_max_ctas)
+        elif self._peer_deltas is not None:
+            self._backward_ctas = torch.cuda.get_device_properties(self.device).multi_processor_count
+        else:
+            self._backward_ctas = self.max_ctas
         if self._hooked:
             return self
         wanted = None if model is None else {id(p) for p in model.parameters()}
@@ -721,10 +735,11 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             return self._shadow, self._shadow_segs, self._shadow_deltas
         return self.flat_weights, self._segs, self._peer_deltas
 
-    def _launch_round(self, r: int, target, g_scale: torch.Tensor | None) -> None:
+    def _launch_round(self, r: int, target, g_scale: torch.Tensor | None, max_ctas: int | None = None) -> None:
         """Round ``r``'s update kernel on the update stream (with the fused all-gather, its peer stores), then
         -- all-gathered by NCCL -- that round's all-gather on the comm stream."""
         weights, segs, deltas = target
+        ctas = self.max_ctas if max_ctas is None else max_ctas
         upd, comm = self._update_stream, self._comm_stream
         start = end = None
         if self.trace is not None:
@@ -732,9 +747,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             start.record(upd)
         if len(segs[r]):
             if self._peer_deltas is not None:
-                self.kernels.multi_step_replicated(upd, segs[r], deltas, self.max_ctas, g_scale)
+                self.kernels.multi_step_replicated(upd, segs[r], deltas, ctas, g_scale)
             else:
-                self.kernels.multi_step(upd, segs[r], self.max_ctas, g_scale)
+                self.kernels.multi_step(upd, segs[r], ctas, g_scale)
         if end is not None:
             end.record(upd)
             self.trace.append((start, end))
@@ -774,7 +789,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         upd, comm = self._update_stream, self._comm_stream
         upd.wait_stream(comm if comm is not None else torch.cuda.current_stream(self.device))
         with torch.cuda.device(self.device):
-            self._launch_round(r, self._target(False), None)
+            self._launch_round(r, self._target(False), None, self._backward_ctas)
         self._rounds_updated.add(r)
 
     def _updates_in_backward(self) -> bool:

@@ -424,7 +424,8 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
     n_params = sum(p.numel() for p in model.parameters())
     opt = ZeroAdamBridge(list(model.parameters()), lr=2e-5, precision="bf16", rounds=args.rounds,
                          gather=args.gather, delay_updates=args.delay, max_ctas=args.max_ctas)
-    opt.attach_hooks(model, update_in_backward=not args.update_at_step)
+    opt.attach_hooks(model, update_in_backward=not args.update_at_step,
+                     backward_max_ctas=args.max_ctas if args.max_ctas > 0 else None)
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     tokens = torch.randint(0, vocab, (batch, seq + 1), device=dev, generator=gen)
     marks = []   # (backward's GPU work done, step done) events of every timed step
