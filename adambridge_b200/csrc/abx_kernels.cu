@@ -1036,7 +1036,8 @@ std::atomic<uint64_t> g_launches{0};
 // space (portable), allocated at the first launch.  Kernels OR failure bits into it with system-scope
 // atomics; the host reads it with no CUDA call.
 std::once_flag g_status_once;
-unsigned int* g_status = nullptr;
+unsigned int* g_status = nullptr;          // host address
+unsigned int* g_status_dev = nullptr;      // its alias in the devices' address space (portable mapping)
 cudaError_t g_status_err = cudaSuccess;
 
 // Failure-path test settings (abx_test_pipeline_fault), copied into the next launches' arguments.
@@ -1054,9 +1055,12 @@ unsigned int* status_word(int* rc)
     std::call_once(g_status_once, [] {
         void* p = nullptr;
         g_status_err = cudaHostAlloc(&p, 64, cudaHostAllocMapped | cudaHostAllocPortable);
+        void* d = nullptr;
+        if (g_status_err == cudaSuccess) g_status_err = cudaHostGetDevicePointer(&d, p, 0);
         if (g_status_err == cudaSuccess) {
+            *static_cast<volatile unsigned int*>(p) = 0;
+            g_status_dev = static_cast<unsigned int*>(d);
             g_status = static_cast<unsigned int*>(p);
-            *reinterpret_cast<volatile unsigned int*>(g_status) = 0;
         }
     });
     if (!g_status) *rc = set_error("allocating the pipeline status word", g_status_err);
@@ -1292,8 +1296,8 @@ int run(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t 
     int rc = ABX_OK;
     DeviceInfo* dev = device_info(&rc);
     if (!dev) return rc;
-    unsigned int* status = status_word(&rc);
-    if (!status) return rc;
+    if (!status_word(&rc)) return rc;
+    unsigned int* status = g_status_dev;   // what the kernels write
     const uint32_t spin_limit = g_spin_limit.load();
     int64_t skip_tile = g_skip_tile.exchange(-1);   // a test's fault applies to the next launch only
     const int lanes = lanes_of(g_simd_level.load());
