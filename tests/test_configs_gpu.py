@@ -11,6 +11,8 @@ element), so a subset of tensors checked whole is a full check of those tensors 
   log-uniform in [1e-4, 1e-2], 50 steps of cosine LR from 2e-5 read from ``param_groups`` every step.
 * C3: Llama-1.5B shapes (1,364,297,728 params), fp8 moments, 1% of gradient entries x100, clip_grad_norm_ 1.0
   fused into the step.
+* C4: Llama-7B shapes (6,738,415,616 params), ZeroLionBridge (world 1) with a bf16 moment, lr 1e-5,
+  betas (0.9, 0.99), weight decay 0.1: the sharded optimizer's flat, round-major state at the full size.
 """
 
 from __future__ import annotations
@@ -44,11 +46,13 @@ def _decoder_shapes(hidden, layers, mlp, vocab, kv, tied, qkv_bias):
 
 QWEN05B = _decoder_shapes(896, 24, 4864, 151936, 128, tied=True, qkv_bias=True)
 LLAMA15B = _decoder_shapes(2048, 24, 5632, 32000, 2048, tied=False, qkv_bias=False)
+LLAMA7B = _decoder_shapes(4096, 32, 11008, 32000, 4096, tied=False, qkv_bias=False)
 
 
 def test_config_shapes_have_the_published_sizes():
     assert sum(math.prod(s) for s in QWEN05B) == 494_032_768
     assert sum(math.prod(s) for s in LLAMA15B) == 1_364_297_728
+    assert sum(math.prod(s) for s in LLAMA7B) == 6_738_415_616
 
 
 def _bf16_params(shapes, seed):
@@ -186,3 +190,44 @@ def test_c3_llama15b_fp8_moments_with_fused_clip():
     for i, hs in host.items():
         _assert_slot_matches(hs, params[i], opt.slots[i], O.DT_FP8)
     opt.close()
+
+
+def _shard_slice(opt, index: int, buf: torch.Tensor) -> torch.Tensor:
+    """Parameter ``index``'s elements gathered, in order, from a world-1 ZeRO shard buffer (round-major pieces)."""
+    parts = sorted((pc.t_lo, buf[pc.local_lo:pc.local_lo + pc.n]) for rnd in opt._pieces for pc in rnd
+                   if pc.index == index)
+    return torch.cat([t for _, t in parts])
+
+
+def test_c4_llama7b_zero_lion_bf16_moment():
+    from adambridge_b200.zero import ZeroLionBridge
+    params = _bf16_params(LLAMA7B, seed=7)
+    opt = ZeroLionBridge(params, lr=1e-5, betas=(0.9, 0.99), weight_decay=0.1, precision="bf16", rounds=4)
+    # checked whole: the embedding and lm_head (131M elements each, cut across rounds), layer-0 q, the last down
+    # projection, a norm
+    per_layer = 9
+    checked = [0, 1, 1 + 31 * per_layer + 6, 1 + 7 * per_layer + 7, len(params) - 1]
+    host = {}
+    for i in checked:
+        p = params[i]
+        hs = O.HostSegment.random(p.numel(), O.DT_BF16, O.DT_BF16, O.DT_BF16, O.DT_F32, O.LION, index=i)
+        hs.buffers["p"] = p.detach().float().cpu().numpy().reshape(-1).copy()
+        host[i] = hs
+    group = _group(1e-5, 0.1, betas=(0.9, 0.99), eps=0.0)
+    orc = O.load_oracle()
+    gen = torch.Generator(device="cuda").manual_seed(14)
+    for step in range(1, 4):
+        for p in params:
+            p.grad = torch.empty(p.shape, dtype=torch.bfloat16, device="cuda").normal_(0.0, 1e-3, generator=gen)
+        for i, hs in host.items():
+            _set_grad(hs, params[i].grad, step)
+        opt.step()
+        assert orc.multi_step([hs.ctype(group) for hs in host.values()], O.SIMD_AVX512) == 0
+        opt.zero_grad(set_to_none=True)
+    torch.cuda.synchronize()
+    for i, hs in host.items():
+        got = hs.clone()
+        got.buffers["out"][:] = params[i].detach().reshape(-1).view(torch.int16).cpu().numpy().view(np.uint16)
+        got.buffers["p"][:] = _shard_slice(opt, i, opt.master.planes["data"]).cpu().numpy()
+        got.buffers["m"][:] = _shard_slice(opt, i, opt.m.planes["data"]).view(torch.int16).cpu().numpy().view(np.uint16)
+        assert got.mismatches(hs) == {}, (i, got.mismatches(hs))
