@@ -1440,6 +1440,25 @@ ABX_API int abx_multi_step_replicated(void* stream, abx_segment* const* segs, in
     return abx::run(stream, segs, nullptr, nsegs, max_ctas, g_scale, out_deltas, nreplicas);
 }
 
+// The copy-engine form of the same all-gather: one asynchronous copy per replica, each on its own stream,
+// so the copy engines move the bytes over NVLink while the SMs go on with the next update.
+ABX_API int abx_replicate_async(void* const* streams, const void* src, int64_t bytes, const int64_t* deltas,
+                                int32_t nreplicas)
+{
+    if (bytes < 0 || nreplicas < 0 || nreplicas > abx::kMaxReplicas) return ABX_E_ARG;
+    if (bytes == 0 || nreplicas == 0) return ABX_OK;
+    if (!src || !deltas || !streams) return ABX_E_NULL_PTR;
+    for (int32_t j = 0; j < nreplicas; ++j)   // a replica may not overlap the source
+        if (deltas[j] > -bytes && deltas[j] < bytes) return ABX_E_ARG;
+    const char* s = static_cast<const char*>(src);
+    for (int32_t j = 0; j < nreplicas; ++j) {
+        const cudaError_t e = cudaMemcpyAsync(const_cast<char*>(s) + deltas[j], s, (size_t)bytes, cudaMemcpyDefault,
+                                              static_cast<cudaStream_t>(streams[j]));
+        if (e != cudaSuccess) return abx::set_error("replica copy", e);
+    }
+    return ABX_OK;
+}
+
 ABX_API int abx_multi_apply_scaled(void* stream, abx_segment* const* segs, const abx_hparams* hps, int32_t nsegs,
                                    int32_t max_ctas, const float* g_scale)
 {

@@ -210,6 +210,9 @@ class NativeKernels:
         lib.abx_multi_step_replicated.restype = ctypes.c_int
         lib.abx_multi_step_replicated.argtypes = [ctypes.c_void_p, seg_array, ctypes.c_int32, ctypes.c_int32,
                                                   ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32]
+        lib.abx_replicate_async.restype = ctypes.c_int
+        lib.abx_replicate_async.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_int64,
+                                            ctypes.POINTER(ctypes.c_int64), ctypes.c_int32]
         lib.abx_multi_apply_scaled.restype = ctypes.c_int
         lib.abx_multi_apply_scaled.argtypes = [ctypes.c_void_p, seg_array, ctypes.POINTER(_HParams), ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_void_p]
@@ -303,6 +306,16 @@ class NativeKernels:
                                                  None if g_scale is None else _scale_ptr(g_scale), deltas,
                                                  len(out_deltas))
         self._check(rc, "abx_multi_step_replicated")
+
+    def replicate_async(self, streams: list, src: int, nbytes: int, deltas: list[int]) -> None:
+        """Copy ``nbytes`` bytes at device address ``src`` to ``src + deltas[j]`` on ``streams[j]`` (copy
+        engines): the all-gather of a sharded update into the peers' copies of a symmetric weight buffer."""
+        if len(streams) != len(deltas):
+            raise ValueError("one stream per replica")
+        hs = (ctypes.c_void_p * max(1, len(streams)))(*[_stream_handle(s) for s in streams])
+        ds = (ctypes.c_int64 * max(1, len(deltas)))(*deltas)
+        rc = self._lib.abx_replicate_async(hs, src, nbytes, ds, len(deltas))
+        self._check(rc, "abx_replicate_async")
 
     def multi_apply(self, stream, segments: ctypes.Array, hparams: list, max_ctas: int = 0,
                     g_scale: torch.Tensor | None = None) -> None:

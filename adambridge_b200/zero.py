@@ -13,8 +13,10 @@ every round::
 
 One step, per round: the rank's update kernel (libabx, writing the new bf16 weights
 straight into its chunk of the flat weight buffer that the parameters view) on the update
-stream, then an in-place NCCL ``all_gather_into_tensor`` of that round on the comm stream.
-The all-gather of round k overlaps the update of round k+1.  ``step()`` first
+stream, then the all-gather of that round: an in-place NCCL ``all_gather_into_tensor`` on
+the comm stream, or -- with the weight buffer in symmetric memory -- copy-engine copies into
+the peers' buffers (``gather='ce'``) or the update kernel's own stores into them
+(``gather='p2p'``).  The all-gather of round k overlaps the update of round k+1.  ``step()`` first
 reduce-scatters (mean) the gradients round by round; ``step_shard(grad_shard)`` takes a
 gradient shard the caller already holds.
 
@@ -143,7 +145,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
     and scattered to their owners (NCCL reduce-scatter), each rank updates its shard, and the new weights are
     all-gathered.  ``gather='p2p'`` (the default where the GPUs can map each other's memory) fuses the
     all-gather into the update: the weight buffer lives in symmetric memory and the kernel stores each new
-    weight into every peer's copy over NVLink; ``'nccl'`` runs NCCL's all-gather round by round instead.
+    weight into every peer's copy over NVLink; ``'ce'`` keeps the symmetric buffer but has the copy engines
+    carry each round's new weights to the peers (one asynchronous copy per peer, overlapping the next round's
+    update); ``'nccl'`` runs NCCL's all-gather round by round instead.
 
     ``delay_updates`` (after ``delay_warmup_steps`` ordinary steps), as the reference's delayed mode: a step's
     update writes a second weight buffer and runs while the caller goes on (the next forward), and it becomes
@@ -187,8 +191,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             raise TypeError(f"parameters must be bfloat16 or float32, got {dtype}")
         self.device, self.dtype = dev, dtype
         self.grad_dtype = grad_dtype or dtype
-        if gather not in ("auto", "p2p", "nccl"):
-            raise ValueError("gather must be 'auto', 'p2p' or 'nccl'")
+        if gather not in ("auto", "p2p", "ce", "nccl"):
+            raise ValueError("gather must be 'auto', 'p2p', 'ce' or 'nccl'")
         if delay_warmup_steps < 0:
             raise ValueError("delay_warmup_steps must be >= 0")
         self.delay_updates, self.delay_warmup_steps = bool(delay_updates), int(delay_warmup_steps)
@@ -196,11 +200,15 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         numels = [p.numel() for p in self._params]
         flat = None
         if self.world > 1 and gather != "nccl":
-            # fused all-gather: nothing to overlap round by round, so one round unless asked otherwise
-            self.layout = FlatLayout(numels, self.world, rounds or 1)
-            flat = self._symmetric_buffer(self.layout.total, dtype, dev, required=gather == "p2p")
+            # fused all-gather: nothing to overlap round by round, so one round unless asked otherwise; the
+            # copy-engine gather overlaps each round's copies with the next round's update
+            self.layout = FlatLayout(numels, self.world, rounds if gather == "ce" else (rounds or 1))
+            flat = self._symmetric_buffer(self.layout.total, dtype, dev, required=gather in ("p2p", "ce"))
         if flat is None:
             self.layout = FlatLayout(numels, self.world, rounds)
+        # the all-gather this optimizer runs (None on one GPU)
+        self.gather = None if self.world == 1 else ("nccl" if flat is None else ("ce" if gather == "ce" else "p2p"))
+        self._replica_streams: list | None = None
         L = self.layout
         with torch.no_grad(), torch.cuda.device(dev):
             if flat is None:
@@ -261,15 +269,18 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             return symm.empty(numel, dtype=dtype, device=dev)
         except Exception as exc:  # noqa: BLE001
             if required:
-                raise RuntimeError(f"gather='p2p' needs symmetric memory: {exc}") from exc
+                raise RuntimeError(f"gather='p2p' and 'ce' need symmetric memory: {exc}") from exc
             return None
+
+    def _rotated_deltas(self, ptrs: list[int]) -> list[int]:
+        """Distances from this rank's buffer to the peers', starting at the next rank: every rank sends to a
+        different peer first, so the NVLink traffic into each GPU is spread over its senders."""
+        return [ptrs[(self.rank + j) % self.world] - ptrs[self.rank] for j in range(1, self.world)]
 
     def _map_peers(self, flat: torch.Tensor) -> None:
         import torch.distributed._symmetric_memory as symm
         self._symm = symm.rendezvous(flat, group=self.pg)
-        ptrs = [int(x) for x in self._symm.buffer_ptrs]
-        base = ptrs[self.rank]
-        self._peer_deltas = [ptrs[r] - base for r in range(self.world) if r != self.rank]
+        self._peer_deltas = self._rotated_deltas([int(x) for x in self._symm.buffer_ptrs])
         self._barrier_flag = torch.zeros(1, dtype=torch.float32, device=flat.device)
 
     def _barrier(self, stream) -> None:
@@ -334,8 +345,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
                 self._shadow = symm.empty(L.total, dtype=self.dtype, device=self.device)
                 self._shadow.zero_()
                 self._symm_shadow = symm.rendezvous(self._shadow, group=self.pg)
-                ptrs = [int(x) for x in self._symm_shadow.buffer_ptrs]
-                self._shadow_deltas = [ptrs[r] - ptrs[self.rank] for r in range(self.world) if r != self.rank]
+                self._shadow_deltas = self._rotated_deltas([int(x) for x in self._symm_shadow.buffer_ptrs])
             else:
                 self._shadow = torch.zeros(L.total, dtype=self.dtype, device=self.device)
         self._shadow_segs = self._build_segments(self._shadow)
@@ -453,7 +463,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             if backward_max_ctas < 0:
                 raise ValueError("backward_max_ctas must be >= 0")
             self._backward_ctas = int(backward_max_ctas)
-        elif self._peer_deltas is not None:
+        elif self.gather == "p2p":
             self._backward_ctas = torch.cuda.get_device_properties(self.device).multi_processor_count
         else:
             self._backward_ctas = self.max_ctas
@@ -685,7 +695,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         target = self._target(delayed)
         self._refresh()
         upd, comm = self._update_stream, self._comm_stream
-        p2p = self._peer_deltas is not None
+        mapped = self._peer_deltas is not None   # the peers write this rank's weight buffer
         upd.wait_stream(cur)
         if comm is not None:
             comm.wait_stream(cur)
@@ -697,7 +707,7 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             h2d.wait_stream(cur)
             d2h.wait_stream(cur)
         with torch.cuda.device(self.device):
-            if p2p and (delayed or had_pending or (flat_grads is None and not synced)):
+            if mapped and (delayed or had_pending or (flat_grads is None and not synced)):
                 self._barrier(upd)   # no peer still reads the weights this update overwrites
             for r in range(L.rounds):
                 if host_in is not None:
@@ -737,7 +747,8 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     def _launch_round(self, r: int, target, g_scale: torch.Tensor | None, max_ctas: int | None = None) -> None:
         """Round ``r``'s update kernel on the update stream (with the fused all-gather, its peer stores), then
-        -- all-gathered by NCCL -- that round's all-gather on the comm stream."""
+        that round's all-gather: the copies of this rank's new weights into the peers' buffers on the replica
+        streams (copy engines), or NCCL's all-gather on the comm stream."""
         weights, segs, deltas = target
         ctas = self.max_ctas if max_ctas is None else max_ctas
         upd, comm = self._update_stream, self._comm_stream
@@ -746,24 +757,44 @@ class ZeroAdamBridge(torch.optim.Optimizer):
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record(upd)
         if len(segs[r]):
-            if self._peer_deltas is not None:
+            if self.gather == "p2p":
                 self.kernels.multi_step_replicated(upd, segs[r], deltas, ctas, g_scale)
             else:
                 self.kernels.multi_step(upd, segs[r], ctas, g_scale)
         if end is not None:
             end.record(upd)
             self.trace.append((start, end))
-        if comm is not None and self._peer_deltas is None:
+        if self.gather == "ce":
+            self._replicate_round(r, weights, deltas)
+        elif self.gather == "nccl":
             L = self.layout
             comm.wait_stream(upd)
             with torch.cuda.stream(comm):
                 dist.all_gather_into_tensor(weights[slice(*L.round_range(r))],
                                             weights[slice(*L.rank_range(r, self.rank))], group=self.pg)
 
+    def _replicate_round(self, r: int, weights: torch.Tensor, deltas: list[int]) -> None:
+        """The copy-engine all-gather of round ``r``: this rank's new weights of the round, once the update
+        stream has written them, copied into each peer's buffer, one replica stream (and copy) per peer."""
+        a, b = self.layout.rank_range(r, self.rank)
+        if b <= a:
+            return
+        if self._replica_streams is None:
+            self._replica_streams = [torch.cuda.Stream(self.device) for _ in range(self.world - 1)]
+        written = torch.cuda.Event()
+        written.record(self._update_stream)
+        for s in self._replica_streams:
+            s.wait_event(written)
+        es = weights.element_size()
+        self.kernels.replicate_async(self._replica_streams, weights.data_ptr() + a * es, (b - a) * es, deltas)
+
     def _finish_update(self, cur, delayed: bool) -> None:
-        """After the last round: every peer's stores have landed (fused all-gather), the step is counted, and
-        -- unless the update is delayed -- the caller's stream is ordered after the update and gathers."""
+        """After the last round: every peer's stores or copies have landed (fused all-gather), the step is
+        counted, and -- unless the update is delayed -- the caller's stream is ordered after the update and
+        gathers."""
         if self._peer_deltas is not None:
+            for s in self._replica_streams or ():
+                self._update_stream.wait_stream(s)   # this rank's copies to the peers are done
             self._barrier(self._update_stream)   # every peer's stores into this rank's weights have landed
         self._steps_done += 1
         self._grads_read, self._grads_read_now = self._grads_read_now, None

@@ -35,6 +35,8 @@ BYTES_PER_PARAM = {("adamw", "bf16"): 20, ("adamw", "fp32"): 28, ("adamw", "fp8"
 # full-size figure is this times the parameters a step updates.
 MEASURED_DRAM_BYTES_PER_PARAM = {("adamw", "bf16"): (2.679388e9 + 2.622009e9) / 267923456,
                                  ("adamw", "fp8"): (2.160363e9 + 2.111521e9) / 267923456}
+# How the new weights reach the other ranks (ZeroAdamBridge.gather), as the bench line names it.
+GATHER_LABELS = {None: None, "p2p": "fused peer stores", "ce": "copy-engine peer copies", "nccl": "nccl"}
 
 
 def llama_shapes(hidden, layers, mlp, vocab, kv, tied=False):
@@ -480,7 +482,7 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
                        "params": n_params, "batch_per_rank": batch, "seq_len": seq, "activation_checkpointing": True,
                        "hooks": True, "delay_updates": args.delay, "parallelism": f"zero1-dp{world}",
                        "rounds": opt.layout.rounds,
-                       "all_gather": ("fused peer stores" if opt._peer_deltas is not None else "nccl") if world > 1 else None},
+                       "all_gather": GATHER_LABELS[opt.gather]},
             "update_kernels_ms": round(upd_ms, 3),
             "exposed_update_ms": round(exposed_ms, 3),
             "exposed_basis": "per step, from the end of backward's GPU work (an event after loss.backward()) to the "
@@ -641,11 +643,12 @@ def sharded_parity(args, world: int, rank: int, dev) -> dict:
     straddling = sum(1 for i in range(len(shapes))
                      if len({r for r in range(world) for rnd in L.pieces(r) for pc in rnd if pc.index == i}) > 1)
     n_checked, n_bad = (int(x) for x in checked.tolist())
+    gather = GATHER_LABELS[zopt.gather]
     del zopt, aopt, zparams, aparams
     torch.cuda.empty_cache()
     return {"checked": n_checked, "mismatches": n_bad, "tensors": len(shapes), "split_over_ranks": straddling,
             "steps": 2, "against": f"world-1 {acls.__name__} on the same tensors and gradients",
-            "gather": "fused peer stores" if world > 1 and args.gather != "nccl" else ("nccl" if world > 1 else None)}
+            "gather": gather}
 
 
 def host_link_gbs(host_g, host_w, opt, world: int, dev, iters: int = 3) -> dict:
@@ -838,7 +841,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     # ---- N > 1: the NVLink reference rate (NCCL's all-gather of the same bytes), then the parity check
     nccl_gbs = nccl_allgather_gbs(opt, world, dev) if world > 1 else None
-    fused_gather = world > 1 and opt._peer_deltas is not None
+    gather_mode = opt.gather
+    fused_gather = gather_mode == "p2p"
     del opt
     torch.cuda.empty_cache()
     parity = None if args.no_parity else sharded_parity(args, world, rank, dev)
@@ -879,7 +883,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
         "config": {"workload": workload_name(dims, algo, prec, args.clip), "params": n_params, "tensors": len(shapes),
                    "weights": "bf16", "grads": "bf16", "master": "fp32", "stochastic_rounding": True,
                    "parallelism": f"zero1-dp{world}", "rounds": L.rounds, "max_ctas": args.max_ctas,
-                   "all_gather": ("fused peer stores" if fused_gather else "nccl") if world > 1 else None,
+                   "all_gather": GATHER_LABELS[gather_mode],
                    "l2": "no flush: each step streams %.1f GB >> 126 MB L2" % (bpp * shard_params / 1e9)},
         "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
@@ -907,7 +911,10 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
         line["allgather"] = {"bytes_received_per_rank": int(received), "step_ms": round(ms_max, 3),
                              "update_kernel_ms": round(kernel_ms_max, 3),
                              "nccl_allgather_gbs": round(nccl_gbs, 1),
+                             "ingress_gbs_over_step": round(received / (ms_max / 1e3) / 1e9, 1),
                              "limited_by": ("NVLink ingress of the update kernel's peer stores" if bound == "nvlink"
+                                            else "NVLink ingress of the copy engines' peer copies"
+                                            if gather_mode == "ce" and received / (ms_max / 1e3) / 1e9 > 0.5 * nccl_gbs
                                             else "HBM traffic of the update kernel")}
     if parity is not None:
         line["parity"] = parity
@@ -934,8 +941,9 @@ def main() -> int:
     ap.add_argument("--rounds", type=int, default=8,
                     help="rounds of the ZeRO layout: the end-to-end step's host copies overlap round by round")
     ap.add_argument("--max-ctas", type=int, default=0, help="cap the update kernel's CTAs (0: every SM)")
-    ap.add_argument("--gather", default="auto", choices=["auto", "p2p", "nccl"],
-                    help="N > 1: all-gather fused into the update as peer stores (p2p), or NCCL's")
+    ap.add_argument("--gather", default="auto", choices=["auto", "p2p", "ce", "nccl"],
+                    help="N > 1: all-gather fused into the update as peer stores (p2p), copy-engine copies into "
+                         "the peers' buffers (ce), or NCCL's")
     ap.add_argument("--layers", type=int, default=None, help="override the decoder depth (small profiling cases)")
     ap.add_argument("--vocab", type=int, default=None, help="override the vocabulary (small profiling cases)")
     ap.add_argument("--clip", type=float, default=None,

@@ -181,6 +181,14 @@ int abx_multi_apply_scaled(void* stream, abx_segment* const* segs, const abx_hpa
 int abx_multi_step_replicated(void* stream, abx_segment* const* segs, int32_t nsegs, int32_t max_ctas,
                               const float* g_scale, const int64_t* out_deltas, int32_t nreplicas);
 
+/* abx_replicate_async: the copy-engine form of that all-gather.  Copies `bytes` bytes at src to
+ * src + deltas[j] (0 <= j < nreplicas <= 7) with one asynchronous copy on streams[j] each, so the
+ * copy engines carry the weights to the peers while the SMs run the next update.  A replica may
+ * not overlap the source (ABX_E_ARG).  The caller orders each stream after the update that wrote
+ * src, and the peers' later reads after the copies.  Not in the reference. */
+int abx_replicate_async(void* const* streams, const void* src, int64_t bytes, const int64_t* deltas,
+                        int32_t nreplicas);
+
 /* Single-tensor AdamW with fp32/bf16 moments and an fp32 master (replaces
  * adambridge_fused_adamw, adambridge_kernels.c:1518, same argument meaning and
  * error codes, plus the stream). */

@@ -177,3 +177,25 @@ def test_convert_rejects_bad_arguments_before_touching_the_device(kernels):
     assert kernels._lib.abx_convert(None, ctypes.byref(bad_src), ctypes.byref(ok_dst), 256) == -1
     assert kernels._lib.abx_convert(None, ctypes.byref(src), ctypes.byref(ok_dst), -1) == -1
     assert kernels._lib.abx_convert(None, ctypes.byref(src), ctypes.byref(ok_dst), 0) == 0
+
+
+def test_replicate_rejects_bad_arguments_before_any_copy(kernels):
+    """abx_replicate_async checks sizes, replica counts, pointers and overlap before issuing a copy (the addresses
+    are never touched, so every rejection comes back on a machine without a GPU)."""
+    lib = kernels._lib
+    streams = (ctypes.c_void_p * 8)(*([None] * 8))
+
+    def deltas(*d):
+        return (ctypes.c_int64 * max(1, len(d)))(*d)
+
+    src = 0x100000
+    assert lib.abx_replicate_async(streams, src, -1, deltas(1 << 20), 1) == -1        # negative size
+    assert lib.abx_replicate_async(streams, src, 64, deltas(*[1 << 20] * 8), 8) == -1  # more than 7 replicas
+    assert lib.abx_replicate_async(streams, src, 64, deltas(1 << 20), -1) == -1
+    assert lib.abx_replicate_async(streams, None, 64, deltas(1 << 20), 1) == -2        # no source
+    assert lib.abx_replicate_async(None, src, 64, deltas(1 << 20), 1) == -2            # no streams
+    assert lib.abx_replicate_async(streams, src, 64, None, 1) == -2                    # no deltas
+    assert lib.abx_replicate_async(streams, src, 64, deltas(1 << 20, 32), 2) == -1     # a replica overlaps src
+    assert lib.abx_replicate_async(streams, src, 64, deltas(-63), 1) == -1
+    assert lib.abx_replicate_async(streams, src, 0, deltas(1 << 20), 1) == 0           # nothing to copy
+    assert lib.abx_replicate_async(streams, src, 64, deltas(), 0) == 0

@@ -16,7 +16,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from adambridge_b200.zero import ALIGN, FlatLayout
+from adambridge_b200.zero import ALIGN, FlatLayout, ZeroAdamBridge
 from oracle import oracle as O
 
 SIZES = [5000, 128, 37, 70001, 4096, 300, 129, 20000]
@@ -48,6 +48,21 @@ def test_layout_covers_every_element_once(world, rounds):
 
 def test_one_round_without_peers():
     assert FlatLayout(SIZES, 1).rounds == 1
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_order_starts_at_the_next_rank(world):
+    """Each rank lists its peers from the next rank on, so at any moment of the gather every GPU receives from a
+    different sender; the distances are those of the peers' buffers."""
+    from types import SimpleNamespace
+    ptrs = [1000 * (r + 1) + 7 * r * r for r in range(world)]
+    firsts = []
+    for rank in range(world):
+        d = ZeroAdamBridge._rotated_deltas(SimpleNamespace(rank=rank, world=world), ptrs)
+        peers = [(rank + j) % world for j in range(1, world)]
+        assert d == [ptrs[p] - ptrs[rank] for p in peers]
+        firsts.append(peers[0])
+    assert sorted(firsts) == list(range(world))
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])

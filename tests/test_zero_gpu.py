@@ -80,7 +80,7 @@ def _rank(rank, world, port, algo, precision, steps, out_dir, gather, clip=None)
         params = _params(f"cuda:{rank}")
         cls = ZeroLionBridge if algo == "lion" else ZeroAdamBridge
         opt = cls(params, lr=1e-3, precision=precision, seed=3, rounds=2, gather=gather)
-        assert (opt._peer_deltas is not None) == (gather == "p2p")
+        assert opt.gather == gather
         for step in range(1, steps + 1):
             for p, g in zip(params, _grads(step, f"cuda:{rank}")):
                 p.grad = g
@@ -96,11 +96,12 @@ def _rank(rank, world, port, algo, precision, steps, out_dir, gather, clip=None)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("gather", ["nccl", "p2p"])
+@pytest.mark.parametrize("gather", ["nccl", "p2p", "ce"])
 @pytest.mark.parametrize("algo,precision", [("adamw", "bf16"), ("adamw", "fp8"), ("lion", "bf16")])
 def test_zero_two_gpus_equals_unsharded(tmp_path, algo, precision, gather):
-    """Reduce-scatter, sharded update and all-gather (NCCL's, or fused into the update as peer stores):
-    every rank ends with the unsharded update's weights, bit for bit."""
+    """Reduce-scatter, sharded update and all-gather (NCCL's, fused into the update as peer stores, or
+    copy-engine copies into the peers' buffers): every rank ends with the unsharded update's weights, bit for
+    bit."""
     steps = 3
     want_w, _ = _reference(algo, precision, steps, "cuda:0")
     mp.start_processes(_rank, args=(2, _free_port(), algo, precision, steps, str(tmp_path), gather), nprocs=2,
@@ -112,7 +113,7 @@ def test_zero_two_gpus_equals_unsharded(tmp_path, algo, precision, gather):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("gather", ["nccl", "p2p"])
+@pytest.mark.parametrize("gather", ["nccl", "p2p", "ce"])
 def test_zero_two_gpus_clip_equals_unsharded(tmp_path, gather):
     """clip_grad_norm_ on the sharded, reduced gradients (per-parameter sums of squares all-reduced) then
     step() == the unsharded AdamBridge's clip_grad_norm_ + step(), on every rank."""
@@ -246,7 +247,7 @@ def _ckpt_rank(rank, world, port, out_dir, gather, saved_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("gather", ["nccl", "p2p"])
+@pytest.mark.parametrize("gather", ["nccl", "p2p", "ce"])
 def test_zero_two_gpus_checkpoint_gather_and_resume(tmp_path, gather):
     """2 ranks: the gathered checkpoint equals the unsharded AdamBridge's; an unsharded checkpoint loaded into
     2 ranks and continued equals the unsharded optimizer continuing."""
@@ -370,7 +371,7 @@ def _hooks_rank(rank, world, port, out_dir, gather, clip):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("gather,clip", [("nccl", None), ("p2p", None), ("p2p", 0.05)])
+@pytest.mark.parametrize("gather,clip", [("nccl", None), ("p2p", None), ("p2p", 0.05), ("ce", None)])
 def test_zero_two_gpus_hooks_equal_step(tmp_path, gather, clip):
     """Reduce-scatters issued from the backward hooks, round by round, give the weights of step()'s
     reduce-scatters on every rank (ranks see different data, so the average matters)."""
@@ -458,7 +459,7 @@ def test_zero_delayed_weights_lag_one_step():
     assert not all(torch.equal(a, b) for a, b in zip(mb.parameters(), after_one))
 
 
-def _delayed_rank(rank, world, port, out_dir):
+def _delayed_rank(rank, world, port, out_dir, gather):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
@@ -467,7 +468,7 @@ def _delayed_rank(rank, world, port, out_dir):
         dev = f"cuda:{rank}"
         ma, mb = _mlp_pair(dev)
         kw = dict(lr=2e-3, precision="bf16", seed=3, rounds=3, delay_updates=True)
-        oa = ZeroAdamBridge(list(ma.parameters()), gather="p2p", **kw)
+        oa = ZeroAdamBridge(list(ma.parameters()), gather=gather, **kw)
         ob = ZeroAdamBridge(list(mb.parameters()), gather="nccl", **kw)
         got = _delayed_run(oa, ma, 4, rank, dev, True)
         want = _delayed_run(ob, mb, 4, rank, dev, False)
@@ -479,12 +480,14 @@ def _delayed_rank(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_zero_two_gpus_delayed_updates():
-    """2 ranks, delayed updates: the fused peer-store gather with hooks and NCCL's gather with step() end with the
-    same weights on every rank."""
+@pytest.mark.parametrize("gather", ["p2p", "ce"])
+def test_zero_two_gpus_delayed_updates(gather):
+    """2 ranks, delayed updates: the gather through symmetric memory (peer stores or copy-engine copies) with
+    hooks and NCCL's gather with step() end with the same weights on every rank."""
     import tempfile
     with tempfile.TemporaryDirectory() as tmp:
-        mp.start_processes(_delayed_rank, args=(2, _free_port(), tmp), nprocs=2, start_method="spawn", join=True)
+        mp.start_processes(_delayed_rank, args=(2, _free_port(), tmp, gather), nprocs=2, start_method="spawn",
+                           join=True)
         ranks = [pickle.load(open(os.path.join(tmp, f"delayed{r}.pkl"), "rb")) for r in range(2)]
     for got, want in ranks:
         assert all(torch.equal(a, b) for a, b in zip(got, want))
