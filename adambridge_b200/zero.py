@@ -452,7 +452,10 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         update stream, and ``step()`` only ends the step; otherwise ``step()`` updates every round.  Delayed
         updates and :meth:`clip_grad_norm_` (which needs every gradient before any update) update at ``step()``:
         pass ``update_in_backward=False`` to clip.  The overlap is per round: construct the optimizer with
-        ``rounds`` > 1 for it.  Every parameter must receive exactly one gradient per step.
+        ``rounds`` > 1 for it.  What the step still waits for after backward is the last round to complete --
+        round 0, holding the first parameters, whose gradients arrive last -- so small rounds pay: Llama-7B on
+        8 B200 leaves 3.4 ms of the update after backward with 32 rounds, 6.7 ms with 8.  Every parameter must
+        receive exactly one gradient per step.
 
         ``backward_max_ctas`` caps the CTAs of the updates run during backward (0: every SM).  By default it is
         one CTA per SM where the all-gather is fused (world > 1): that update waits on NVLink, and leaving SMs to

@@ -424,7 +424,7 @@ def train_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
     with torch.device(dev):
         model = Decoder().to(torch.bfloat16)
     n_params = sum(p.numel() for p in model.parameters())
-    opt = ZeroAdamBridge(list(model.parameters()), lr=2e-5, precision="bf16", rounds=args.rounds,
+    opt = ZeroAdamBridge(list(model.parameters()), lr=2e-5, precision="bf16", rounds=args.rounds or 32,
                          gather=args.gather, delay_updates=args.delay, max_ctas=args.max_ctas)
     opt.attach_hooks(model, update_in_backward=not args.update_at_step,
                      backward_max_ctas=args.max_ctas if args.max_ctas > 0 else None)
@@ -756,7 +756,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> dict | None:
     cls = ZeroLionBridge if algo == "lion" else ZeroAdamBridge
     kw = dict(lr=1e-5, betas=(0.9, 0.99), weight_decay=0.1) if algo == "lion" else \
         dict(lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
-    opt = cls(params, precision=prec, rounds=args.rounds, max_ctas=args.max_ctas, gather=args.gather, **kw)
+    opt = cls(params, precision=prec, rounds=args.rounds or 8, max_ctas=args.max_ctas, gather=args.gather, **kw)
     L = opt.layout
     shard_params = sum(pc.n for r in opt._pieces for pc in r)
     with torch.no_grad():
@@ -938,8 +938,10 @@ def main() -> int:
                     help="--workload convert: the source format (the destination is --precision)")
     ap.add_argument("--algorithm", default="adamw", choices=["adamw", "lion"])
     ap.add_argument("--precision", default="bf16", choices=["fp32", "bf16", "fp8"])
-    ap.add_argument("--rounds", type=int, default=8,
-                    help="rounds of the ZeRO layout: the end-to-end step's host copies overlap round by round")
+    ap.add_argument("--rounds", type=int, default=None,
+                    help="rounds of the ZeRO layout (default: 8 for the update, whose end-to-end host copies "
+                         "overlap round by round; 32 for the training step, whose last round's update is what "
+                         "the step still waits for after backward)")
     ap.add_argument("--max-ctas", type=int, default=0, help="cap the update kernel's CTAs (0: every SM)")
     ap.add_argument("--gather", default="auto", choices=["auto", "p2p", "ce", "nccl"],
                     help="N > 1: all-gather fused into the update as peer stores (p2p), copy-engine copies into "
