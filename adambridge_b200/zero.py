@@ -151,7 +151,9 @@ class ZeroAdamBridge(torch.optim.Optimizer):
 
     ``delay_updates`` (after ``delay_warmup_steps`` ordinary steps), as the reference's delayed mode: a step's
     update writes a second weight buffer and runs while the caller goes on (the next forward), and it becomes
-    the weights at the next step -- the model trains with weights one step stale.  ``flush()`` applies it.
+    the weights at the next step -- the model trains with weights one step stale.  ``flush()`` applies it.  The
+    parameters' storage then alternates between the two buffers (applying an update re-points them, copying
+    nothing), so code should not keep views of a parameter's storage from one step to the next.
 
     ``step_shard(grad_shard)``: the caller supplies this rank's already reduced gradient shard
     (``shard_numel`` elements, round-major; see :class:`FlatLayout`).  Every parameter is updated every step.
@@ -351,14 +353,25 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         self._shadow_segs = self._build_segments(self._shadow)
 
     def _apply_pending(self, cur) -> None:
-        """The previous step's delayed update becomes the weights (on ``cur``, after that update and its gather)."""
+        """The previous step's delayed update becomes the weights (on ``cur``, after that update and its gather).
+
+        The two weight buffers trade places instead of copying 2 bytes per parameter twice: the parameters now
+        view the buffer that update wrote, and the next delayed update writes the other one, after the work
+        already enqueued on ``cur`` (which still reads it) and, with peers writing it, after the step's opening
+        barrier.  Every rank trades at the same step, so the peers' buffers trade alike."""
         if not self._delay_owed:
             return
         cur.wait_stream(self._update_stream)
         if self._comm_stream is not None:
             cur.wait_stream(self._comm_stream)
+        self.flat_weights, self._shadow = self._shadow, self.flat_weights
+        self._segs, self._shadow_segs = self._shadow_segs, self._segs
+        self._peer_deltas, self._shadow_deltas = self._shadow_deltas, self._peer_deltas
+        L = self.layout
         with torch.no_grad():
-            self.flat_weights.copy_(self._shadow)
+            for i, p in enumerate(self._params):
+                a, b = L.flat_slice(i)
+                p.data = self.flat_weights[a:b].view(p.shape)
         self._delay_owed = False
 
     def _after_grad_reads(self, stream) -> None:
