@@ -74,3 +74,13 @@ def test_flags_parse():
     for flag in ("--gpus", "--steps", "--warmup", "--impl", "--workload", "--algorithm", "--precision", "--rounds",
                  "--gather", "--clip", "--no-e2e", "--no-cpu-baseline", "--no-parity", "--cpu-variant-seconds"):
         assert flag in p.stdout, flag
+
+
+def test_gather_labels_cover_every_mode():
+    """Every all-gather a ZeRO optimizer can run (and none, on one GPU) has the name the bench line prints, and
+    the flag offers each mode."""
+    import bench
+    assert set(bench.GATHER_LABELS) == {None, "p2p", "ce", "nccl"}
+    p = subprocess.run([sys.executable, "bench.py", "--help"], cwd=ROOT, capture_output=True, text=True, timeout=120)
+    for mode in ("auto", "p2p", "ce", "nccl"):
+        assert mode in p.stdout
