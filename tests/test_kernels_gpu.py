@@ -295,3 +295,56 @@ def test_fp8_codec_wide_dynamic_range(kernels, oracle, algo, sr):
 def test_pipeline_status_clear_after_all_updates(kernels):
     """No bounded pipeline wait gave up in any update of this session (the status word is still zero)."""
     assert kernels.pipeline_status() == 0
+
+
+@pytest.mark.parametrize("prec", [O.DT_BF16, O.DT_FP8])
+def test_ema_stall_known_answer(kernels, oracle, prec):
+    """The reference's EMA-stall known answer (tests/test_precision.py:99-123) through the GPU kernel: 500 steps of
+    v <- 0.999 v + 0.001 g^2 (AdamW with b1 = 0, g^2 = 1.5 every step, v starting at 1).  Round-to-nearest
+    moments freeze at 1 (bf16) or near it (FP8); stochastic rounding tracks the exact EMA (~1.197).  Every step
+    runs on the GPU and in the oracle, and the final second moments agree bit for bit."""
+    n = 4096
+    target = np.full(n, 1.5, np.float32)
+    target[::128] = 4.0          # one larger value per block, so FP8 block scales stay put
+    tracked = np.ones(n, bool)
+    tracked[::128] = False
+    kernels.set_simd_level("scalar")
+    try:
+        results = _ema_runs(kernels, oracle, prec, n, target, tracked)
+    finally:
+        kernels.set_simd_level(None)
+    exact = 1.5 + (1.0 - 1.5) * 0.999 ** 500
+    assert results[0] == pytest.approx(1.0, abs=1e-6) if prec == O.DT_BF16 else results[0] < 1.1
+    assert results[1] == pytest.approx(exact, rel=0.01 if prec == O.DT_BF16 else 0.03)
+
+
+def _ema_runs(kernels, oracle, prec, n, target, tracked):
+    from adambridge_b200 import native
+    results = {}
+    for sr in (0, 1):
+        hs = O.HostSegment.random(n, O.DT_F32, prec, O.DT_NONE, O.DT_F32, O.ADAMW, seed=1)
+        hs.buffers["g"][:] = np.sqrt(target)
+        init = np.ones(n, np.float32)
+        init[::128] = 4.0
+        if prec == O.DT_BF16:
+            hs.buffers["v"][:] = O.bf16_bits(init)
+        else:
+            scale = np.float32(2.0) / np.float32(57344.0)
+            hs.buffers["v_scale"][:] = scale
+            hs.buffers["v"][:] = [oracle.fp8_encode(float(np.float32(x / scale)), 0, 0, "v") for x in np.sqrt(init)]
+        dev = to_device(hs)
+        arr = kernels.segment_array([ctypes.pointer(device_segment(hs, dev))])
+        for step in range(1, 501):
+            seed = oracle.step_seed(0, 0, step)
+            h = O.HParams(0.0, 0.999, 1.0, np.float32(1 - 0.999), 1.0, 0.0, 1.0, 1e-8, seed, sr)
+            kernels.multi_apply(None, arr, [native._HParams(*[getattr(h, f) for f, _ in O.HParams._fields_])])
+            assert oracle.multi_apply([hs.ctype()], [h], O.SIMD_SCALAR) == 0
+        got = from_device(hs, dev)
+        assert not got.mismatches(hs), got.mismatches(hs)
+        if prec == O.DT_BF16:
+            v = O.bf16_to_f32(got.buffers["v"])
+        else:
+            v = np.array([oracle.fp8_decode(int(c), "v") for c in got.buffers["v"][:n]], np.float32)
+            v = (v * np.repeat(got.buffers["v_scale"], 128)[:n]) ** 2
+        results[sr] = float(v[tracked].mean())
+    return results
