@@ -471,15 +471,17 @@ class ZeroAdamBridge(torch.optim.Optimizer):
         receive exactly one gradient per step.
 
         ``backward_max_ctas`` caps the CTAs of the updates run during backward (0: every SM).  By default it is
-        one CTA per SM where the all-gather is fused (world > 1): that update waits on NVLink, and leaving SMs to
-        the backward pass shortens the step (Llama-7B on 8 B200: 288.4 ms per step against 292.4 ms uncapped);
-        on one GPU, where the update is HBM-bound, the constructor's ``max_ctas`` applies."""
+        one CTA per SM where the all-gather is fused and the update waits on NVLink (4 or more ranks): leaving SMs
+        to the backward pass shortens the step (Llama-7B on 8 B200: 288.4 ms per step against 292.4 ms
+        uncapped, 8 rounds).  With fewer ranks the update is HBM-bound and a cap only stretches it (2 B200: the
+        capped update kernels took 37.2 ms of a 293.1 ms step, 14.5 ms uncapped), so the constructor's
+        ``max_ctas`` applies."""
         self._update_in_backward = bool(update_in_backward)
         if backward_max_ctas is not None:
             if backward_max_ctas < 0:
                 raise ValueError("backward_max_ctas must be >= 0")
             self._backward_ctas = int(backward_max_ctas)
-        elif self.gather == "p2p":
+        elif self.gather == "p2p" and self.world >= 4:
             self._backward_ctas = torch.cuda.get_device_properties(self.device).multi_processor_count
         else:
             self._backward_ctas = self.max_ctas
